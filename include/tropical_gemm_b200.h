@@ -1,0 +1,124 @@
+/*
+ * tropical_gemm_b200.h -- C ABI of the B200-native tropical GEMM engine.
+ *
+ * C = A (x) B over a tropical semiring, optionally with the argmax index of
+ * the winning k for every output, plus the argmax-scatter backward pass.
+ *
+ * Conventions shared by every entry point
+ *   - All pointers are device pointers (cudaMalloc / torch CUDA storage),
+ *     except where a comment says otherwise.  The library never allocates
+ *     outputs: the caller passes C, argmax and gradient buffers.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy
+ *     default stream.  Every call is stream-ordered and asynchronous: no
+ *     host synchronisation happens inside the library.
+ *   - Leading dimensions (lda/ldb/ldc) are in elements.  For TG_ROW_MAJOR
+ *     A is M x K with A[i,k] at a[i*lda + k]; for TG_COL_MAJOR A[i,k] is at
+ *     a[k*lda + i] (the column-major convention of the reference's Rust
+ *     GPU API).  The same layout applies to B, C and argmax.
+ *   - argmax is int32 with the same leading dimension as C; NULL selects
+ *     the plain (value-only) GEMM.
+ *   - Semantics follow the reference bit for bit: k is visited in
+ *     ascending order, the accumulator starts at the semiring zero with
+ *     index 0, and a product replaces it only when strictly better, so the
+ *     lowest k among ties wins and outputs that nothing beats keep index 0.
+ *     Integer MaxPlus/MinPlus use the sentinels -46340/+46340 (i32) and
+ *     -3037000499/+3037000499 (i64) with the reference's saturating add.
+ *   - Return value: TG_OK or an error code; tg_last_error() gives a
+ *     human-readable message for the calling thread.
+ */
+#ifndef TROPICAL_GEMM_B200_H
+#define TROPICAL_GEMM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum { TG_MAXPLUS = 0, TG_MINPLUS = 1, TG_MAXMUL = 2 } tg_semiring;
+typedef enum { TG_F32 = 0, TG_F64 = 1, TG_I32 = 2, TG_I64 = 3 } tg_dtype;
+typedef enum { TG_ROW_MAJOR = 0, TG_COL_MAJOR = 1 } tg_layout;
+
+typedef enum {
+  TG_OK = 0,
+  TG_ERR_INVALID_ARGUMENT = 1,  /* null pointer, negative size, bad enum   */
+  TG_ERR_DIMENSION_MISMATCH = 2,/* leading dimension too small, etc.       */
+  TG_ERR_UNSUPPORTED = 3,       /* combination not provided (e.g. int grad) */
+  TG_ERR_CUDA = 4,              /* a CUDA runtime call failed              */
+  TG_ERR_NO_DEVICE = 5          /* no CUDA device visible                  */
+} tg_status;
+
+/* Library version string, e.g. "0.2.0-b200". */
+const char* tg_version(void);
+
+/* Message describing the last failing call on this thread ("" if none). */
+const char* tg_last_error(void);
+
+/* Number of visible CUDA devices (0 when none); never fails.
+ * Replaces cuda_device_count (crates/tropical-gemm-cuda/src/lib.rs:63). */
+int tg_device_count(void);
+
+/* C = A (x) B, optionally with argmax.
+ * Replaces CudaKernel::launch_gemm and CudaKernelWithArgmax::launch_gemm_with_argmax
+ * (crates/tropical-gemm-cuda/src/kernels.rs:22-27, :202-207), the free functions
+ * tropical_matmul_gpu[_with_argmax] / tropical_gemm_gpu[_with_argmax]
+ * (crates/tropical-gemm-cuda/src/lib.rs:221, :256, :354, :392), and the DLPack
+ * launchers launch_gemm_external[_with_argmax]_f32 (kernels.rs:388-473).
+ * M, N or K equal to 0 is accepted: with K == 0 every output is the semiring
+ * zero with index 0; with M or N == 0 nothing is written. */
+tg_status tg_gemm(tg_semiring semiring, tg_dtype dtype, tg_layout layout,
+                  int64_t m, int64_t n, int64_t k,
+                  const void* a, int64_t lda,
+                  const void* b, int64_t ldb,
+                  void* c, int64_t ldc,
+                  int32_t* argmax,
+                  void* stream);
+
+/* Strided batched GEMM: for p in [0, batch) computes
+ * C[p] = A[p] (x) B[p] with A[p] = a + p*stride_a (elements), etc.;
+ * argmax uses stride_c.  One launch for the whole batch.
+ * Replaces launch_gemm_external_batched_with_argmax_f32 (kernels.rs:498-550)
+ * and tropical_matmul_gpu_strided_batched[_with_argmax]
+ * (crates/tropical-gemm-cuda/src/lib.rs:486, :563, :1007). */
+tg_status tg_gemm_strided_batched(tg_semiring semiring, tg_dtype dtype, tg_layout layout,
+                                  int64_t batch, int64_t m, int64_t n, int64_t k,
+                                  const void* a, int64_t lda, int64_t stride_a,
+                                  const void* b, int64_t ldb, int64_t stride_b,
+                                  void* c, int64_t ldc, int64_t stride_c,
+                                  int32_t* argmax,
+                                  void* stream);
+
+/* Backward pass w.r.t. A:
+ *   grad_a[i, argmax[i,j]] += grad_c[i,j] * w[i,j]
+ * where w = 1 for MaxPlus/MinPlus and w = B[argmax[i,j], j] for MaxMul
+ * (the multiplicative rule of pytorch.py:521-548; pass b for MaxMul, NULL
+ * otherwise).  Indices outside [0, K) are skipped, as in the reference kernel.
+ * accumulate == 0 overwrites grad_a (no pre-zeroing needed); != 0 adds into it.
+ * Float types only.  Replaces tropical_backward_a_gpu_kernel
+ * (crates/tropical-gemm-cuda/src/lib.rs:841-882) and the torch scatter_add_
+ * backward (crates/tropical-gemm-python/python/tropical_gemm/pytorch.py:386-403). */
+tg_status tg_backward_a(tg_semiring semiring, tg_dtype dtype, tg_layout layout,
+                        int64_t batch, int64_t m, int64_t n, int64_t k,
+                        const void* grad_c, int64_t ldc, int64_t stride_c,
+                        const int32_t* argmax,
+                        const void* b, int64_t ldb, int64_t stride_b,
+                        void* grad_a, int64_t lda, int64_t stride_a,
+                        int accumulate, void* stream);
+
+/* Backward pass w.r.t. B:
+ *   grad_b[argmax[i,j], j] += grad_c[i,j] * w[i,j]
+ * with w = 1, or A[i, argmax[i,j]] for MaxMul (pass a).  Same conventions
+ * as tg_backward_a.  Replaces tropical_backward_b_gpu_kernel
+ * (crates/tropical-gemm-cuda/src/lib.rs:901-942). */
+tg_status tg_backward_b(tg_semiring semiring, tg_dtype dtype, tg_layout layout,
+                        int64_t batch, int64_t m, int64_t n, int64_t k,
+                        const void* grad_c, int64_t ldc, int64_t stride_c,
+                        const int32_t* argmax,
+                        const void* a, int64_t lda, int64_t stride_a,
+                        void* grad_b, int64_t ldb, int64_t stride_b,
+                        int accumulate, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TROPICAL_GEMM_B200_H */

@@ -1,0 +1,204 @@
+"""GPU parity: the engine's forward kernels against the CPU oracle, bit-exact
+(values and argmax), for every semiring x dtype, both layouts, odd shapes,
+ties, special values, batching and edge cases the reference tests."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import SEMIS, engine, engine_colmajor, oracle, same_bits, dev
+from tropical_gemm import _native as N
+
+pytestmark = pytest.mark.gpu
+
+FIX = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_fixtures.npz"))
+NAMES = [str(n) for n in FIX["__names__"]]
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_reference_fixtures_on_gpu(name):
+    a, b = FIX[name + "__a"], FIX[name + "__b"]
+    c, am = engine(name.split("_")[0], a, b)
+    assert same_bits(c, FIX[name + "__c"])
+    assert np.array_equal(am, FIX[name + "__argmax"])
+
+
+@pytest.mark.parametrize("name", [n for n in NAMES if "batched" not in n])
+def test_reference_fixtures_colmajor(name):
+    a, b = FIX[name + "__a"], FIX[name + "__b"]
+    c, am = engine_colmajor(name.split("_")[0], a, b)
+    assert same_bits(c, FIX[name + "__c"])
+    assert np.array_equal(am, FIX[name + "__argmax"])
+
+
+def _data(rng, dtype, shape, kind):
+    if kind == "normal":
+        if np.issubdtype(dtype, np.floating):
+            return rng.standard_normal(shape).astype(dtype)
+        return rng.integers(-1000, 1000, shape).astype(dtype)
+    if kind == "ties":  # few distinct values -> many exact ties
+        return rng.integers(-3, 4, shape).astype(dtype)
+    raise ValueError(kind)
+
+
+SHAPES = [(1, 1, 1), (7, 13, 5), (63, 65, 127), (129, 130, 257), (200, 3, 70), (128, 128, 32), (1, 300, 1000)]
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.int32, np.int64])
+@pytest.mark.parametrize("kind", ["normal", "ties"])
+@pytest.mark.parametrize("with_argmax", [True, False])
+def test_random_shapes(semi, dtype, kind, with_argmax):
+    rng = np.random.default_rng(hash((semi, str(dtype), kind)) % 2**32)
+    for (m, k, n) in SHAPES:
+        a = _data(rng, dtype, (m, k), kind)
+        b = _data(rng, dtype, (k, n), kind)
+        c, am = engine(semi, a, b, with_argmax)
+        c0, am0 = oracle(semi, a, b, with_argmax)
+        assert same_bits(c, c0), f"values differ at {(m, k, n)}"
+        if with_argmax:
+            assert np.array_equal(am, am0), f"argmax differs at {(m, k, n)}"
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+def test_colmajor_random(semi):
+    rng = np.random.default_rng(5)
+    for dtype in (np.float32, np.float64, np.int32):
+        a = _data(rng, dtype, (77, 45), "ties")
+        b = _data(rng, dtype, (45, 91), "ties")
+        c, am = engine_colmajor(semi, a, b)
+        c0, am0 = oracle(semi, a, b)
+        assert same_bits(c, c0) and np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("k", [1, 2, 3, 4, 31, 32, 33, 63, 64, 65, 100, 511, 1000])
+def test_fast_path_k_tails(semi, k):
+    rng = np.random.default_rng(k)
+    a = rng.standard_normal((130, k)).astype(np.float32)
+    b = rng.standard_normal((k, 140)).astype(np.float32)
+    for wa in (True, False):
+        c, am = engine(semi, a, b, wa)
+        c0, am0 = oracle(semi, a, b, wa)
+        assert same_bits(c, c0)
+        if wa:
+            assert np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+def test_fast_path_many_chunks(semi):
+    """K large enough that the chunk length grows (more than 1024 chunks of 64)."""
+    rng = np.random.default_rng(11)
+    k = 70000
+    a = rng.integers(-50, 50, (20, k)).astype(np.float32)
+    b = rng.integers(-50, 50, (k, 24)).astype(np.float32)
+    c, am = engine(semi, a, b)
+    c0, am0 = oracle(semi, a, b)
+    assert same_bits(c, c0) and np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+def test_special_values_fast_and_generic(semi):
+    rng = np.random.default_rng(3)
+    for dtype in (np.float32, np.float64):
+        a = rng.standard_normal((150, 97)).astype(dtype)
+        b = rng.standard_normal((97, 133)).astype(dtype)
+        for arr in (a, b):
+            mask = rng.random(arr.shape)
+            arr[mask < 0.05] = np.inf
+            arr[(mask >= 0.05) & (mask < 0.10)] = -np.inf
+            arr[(mask >= 0.10) & (mask < 0.13)] = np.nan
+            arr[(mask >= 0.13) & (mask < 0.18)] = 0.0
+            arr[(mask >= 0.18) & (mask < 0.23)] = -0.0
+        for wa in (True, False):
+            c, am = engine(semi, a, b, wa)
+            c0, am0 = oracle(semi, a, b, wa)
+            assert same_bits(c, c0)
+            if wa:
+                assert np.array_equal(am, am0)
+
+
+def test_minplus_sparse_graph_distances():
+    """BASELINE config 2b shape at reduced size: 90% +inf, values in [0,100)."""
+    rng = np.random.default_rng(1)
+    mats = []
+    for _ in range(2):
+        v = (100 * rng.random((300, 300))).astype(np.float32)
+        v[rng.random((300, 300)) < 0.9] = np.inf
+        mats.append(v)
+    c, am = engine("minplus", *mats)
+    c0, am0 = oracle("minplus", *mats)
+    assert same_bits(c, c0) and np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", ["minplus", "maxplus"])
+def test_integer_sentinels_on_gpu(semi):
+    rng = np.random.default_rng(7)
+    for dtype, inf in ((np.int32, 46340), (np.int64, 3037000499)):
+        a = rng.integers(0, 1000, (90, 70)).astype(dtype)
+        b = rng.integers(0, 1000, (70, 80)).astype(dtype)
+        s = inf if semi == "minplus" else -inf
+        a[rng.random(a.shape) < 0.5] = s
+        b[rng.random(b.shape) < 0.5] = s
+        if semi == "maxplus":
+            a, b = np.where(a == s, a, -a), np.where(b == s, b, -b)
+        c, am = engine(semi, a, b)
+        c0, am0 = oracle(semi, a, b)
+        assert same_bits(c, c0) and np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.int32])
+def test_batched(semi, dtype):
+    rng = np.random.default_rng(9)
+    for (bs, m, k, n) in [(3, 8, 8, 8), (5, 65, 33, 70), (2, 130, 300, 129)]:
+        a = _data(rng, dtype, (bs, m, k), "ties")
+        b = _data(rng, dtype, (bs, k, n), "ties")
+        c, am = engine(semi, a, b)
+        c0, am0 = oracle(semi, a, b)
+        assert same_bits(c, c0) and np.array_equal(am, am0)
+
+
+def test_k_zero_gives_semiring_zero_and_index_zero():
+    for semi, z in (("maxplus", -np.inf), ("minplus", np.inf), ("maxmul", 0.0)):
+        a = torch.empty((5, 0), device=dev())
+        b = torch.empty((0, 6), device=dev())
+        c, am = N.gemm(semi, a, b, True)
+        assert (c.cpu().numpy() == z).all() and (am.cpu().numpy() == 0).all()
+
+
+def test_empty_m_or_n():
+    a = torch.zeros((0, 4), device=dev())
+    b = torch.zeros((4, 3), device=dev())
+    c, am = N.gemm("maxplus", a, b, True)
+    assert c.shape == (0, 3)
+
+
+def test_unaligned_leading_dimension_uses_exact_path():
+    """lda not a multiple of 4 (a padded buffer): generic kernel, same bits."""
+    rng = np.random.default_rng(4)
+    m, k, n = 70, 37, 50
+    buf = rng.standard_normal((m, k + 1)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    ta = torch.from_numpy(buf).to(dev())
+    tb = torch.from_numpy(b).to(dev())
+    c = torch.empty((m, n), device=dev())
+    am = torch.empty((m, n), dtype=torch.int32, device=dev())
+    N.check(N.lib().tg_gemm(0, 0, 0, m, n, k, ta.data_ptr(), k + 1, tb.data_ptr(), n, c.data_ptr(), n,
+                            am.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    c0, am0 = oracle("maxplus", np.ascontiguousarray(buf[:, :k]), b)
+    assert same_bits(c.cpu().numpy(), c0) and np.array_equal(am.cpu().numpy(), am0)
+
+
+def test_large_square_vs_oracle_sampled_rows():
+    """2048^2 x 1024 on the fast path, checked on a sample of rows (full rows, all k)."""
+    rng = np.random.default_rng(1)
+    m, k, n = 2048, 1024, 2048
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((k, n), dtype=np.float32)
+    c, am = engine("maxplus", a, b)
+    rows = rng.choice(m, 64, replace=False)
+    c0, am0 = oracle("maxplus", a[rows], b)
+    assert same_bits(c[rows], c0) and np.array_equal(am[rows], am0)

@@ -1,0 +1,333 @@
+// C ABI of the engine: validation, layout mapping and kernel dispatch.
+// Declarations and per-function contracts live in include/tropical_gemm_b200.h.
+//
+// Host-side responsibilities (the reference's cu/src/{kernels,lib}.rs):
+//  * shape / leading-dimension / pointer checks with error codes instead
+//    of Rust `Result`s (crates/tropical-gemm-cuda/src/error.rs:8-29);
+//  * column-major callers become the canonical row-major problem
+//    C^T = B^T (x) A^T by swapping operands and M <-> N -- the same trick
+//    the reference applies for row-major DLPack tensors (kernels.rs:416-430),
+//    here in the opposite direction;
+//  * kernel choice: the f32 fast path when alignment allows, else the
+//    generic exact kernel;
+//  * stream-ordered launches only: no allocation, no synchronisation.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <algorithm>
+#include <cuda_runtime.h>
+#include "../../include/tropical_gemm_b200.h"
+#include "tg_semiring.cuh"
+#include "tg_generic.cuh"
+#include "tg_fast_f32.cuh"
+#include "tg_backward.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+tg_status fail(tg_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+tg_status fail(tg_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+tg_status check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return TG_OK;
+}
+
+template <int S, typename T>
+__global__ void fill_zero_kernel(T* c, int32_t* idx, int64_t m, int64_t n, int64_t ldc, int64_t sc) {
+  using R = tg::Ring<S, T>;
+  T* cb = c + int64_t(blockIdx.y) * sc;
+  int32_t* ib = idx ? idx + int64_t(blockIdx.y) * sc : nullptr;
+  const int64_t total = m * n;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t o = (e / n) * ldc + e % n;
+    cb[o] = R::zero();
+    if (ib) ib[o] = 0;
+  }
+}
+
+struct Problem {
+  tg::GemmArgs g;
+  int64_t batch;
+};
+
+bool fast_f32_ok(const Problem& P) {
+  const auto& g = P.g;
+  if ((reinterpret_cast<uintptr_t>(g.a) & 15) != 0) return false;
+  if (g.lda % 4 != 0) return false;
+  if (P.batch > 1 && g.sa % 4 != 0) return false;
+  if (g.k >= (int64_t(1) << 31)) return false;
+  return true;
+}
+
+template <int S, bool ARGMAX>
+tg_status launch_fast_f32(const Problem& P, cudaStream_t st) {
+  auto kern = tg::fast_f32_kernel<S, ARGMAX>;
+  const size_t smem = ARGMAX ? tg::kFSmemArgmax : tg::kFSmemValues;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return fail(TG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
+  int tpc = 2;
+  while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
+  const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;
+  const int64_t gy = (P.g.n + tg::kFBN - 1) / tg::kFBN;
+  if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
+  for (int64_t b0 = 0; b0 < P.batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
+    tg::GemmArgs g = P.g;
+    g.a = static_cast<const float*>(g.a) + b0 * g.sa;
+    g.b = static_cast<const float*>(g.b) + b0 * g.sb;
+    g.c = static_cast<float*>(g.c) + b0 * g.sc;
+    if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc);
+    tg_status s = check_launch("fast_f32_kernel launch");
+    if (s != TG_OK) return s;
+  }
+  return TG_OK;
+}
+
+template <int S, typename T, bool ARGMAX>
+tg_status launch_generic(const Problem& P, cudaStream_t st) {
+  const int64_t gx = (P.g.m + tg::kGenBM - 1) / tg::kGenBM;
+  const int64_t gy = (P.g.n + tg::kGenBN - 1) / tg::kGenBN;
+  if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
+  for (int64_t b0 = 0; b0 < P.batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
+    tg::GemmArgs g = P.g;
+    g.a = static_cast<const T*>(g.a) + b0 * g.sa;
+    g.b = static_cast<const T*>(g.b) + b0 * g.sb;
+    g.c = static_cast<T*>(g.c) + b0 * g.sc;
+    if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
+    tg::generic_gemm_kernel<S, T, ARGMAX><<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kGenThreads, 0, st>>>(g);
+    tg_status s = check_launch("generic_gemm_kernel launch");
+    if (s != TG_OK) return s;
+  }
+  return TG_OK;
+}
+
+template <int S, typename T>
+tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
+  const bool am = P.g.argmax != nullptr;
+  if (P.g.k == 0) {
+    for (int64_t b0 = 0; b0 < P.batch; b0 += 65535) {
+      const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
+      fill_zero_kernel<S, T><<<dim3(256, unsigned(nb)), 256, 0, st>>>(
+          static_cast<T*>(P.g.c) + b0 * P.g.sc, am ? P.g.argmax + b0 * P.g.sc : nullptr,
+          P.g.m, P.g.n, P.g.ldc, P.g.sc);
+      tg_status s = check_launch("fill_zero_kernel launch");
+      if (s != TG_OK) return s;
+    }
+    return TG_OK;
+  }
+  if constexpr (std::is_same<T, float>::value) {
+    if (fast_f32_ok(P)) return am ? launch_fast_f32<S, true>(P, st) : launch_fast_f32<S, false>(P, st);
+  }
+  return am ? launch_generic<S, T, true>(P, st) : launch_generic<S, T, false>(P, st);
+}
+
+template <typename T>
+tg_status dispatch_semiring(tg_semiring s, const Problem& P, cudaStream_t st) {
+  switch (s) {
+    case TG_MAXPLUS: return dispatch_typed<tg::kMaxPlus, T>(P, st);
+    case TG_MINPLUS: return dispatch_typed<tg::kMinPlus, T>(P, st);
+    case TG_MAXMUL: return dispatch_typed<tg::kMaxMul, T>(P, st);
+  }
+  return fail(TG_ERR_INVALID_ARGUMENT, "unknown semiring %d", int(s));
+}
+
+size_t dtype_size(tg_dtype t) {
+  switch (t) {
+    case TG_F32: case TG_I32: return 4;
+    case TG_F64: case TG_I64: return 8;
+  }
+  return 0;
+}
+
+tg_status gemm_impl(tg_semiring semiring, tg_dtype dtype, tg_layout layout, int64_t batch,
+                    int64_t m, int64_t n, int64_t k, const void* a, int64_t lda, int64_t sa,
+                    const void* b, int64_t ldb, int64_t sb, void* c, int64_t ldc, int64_t sc,
+                    int32_t* argmax, void* stream) {
+  g_last_error.clear();
+  if (semiring < TG_MAXPLUS || semiring > TG_MAXMUL) return fail(TG_ERR_INVALID_ARGUMENT, "unknown semiring %d", int(semiring));
+  if (dtype_size(dtype) == 0) return fail(TG_ERR_INVALID_ARGUMENT, "unknown dtype %d", int(dtype));
+  if (layout != TG_ROW_MAJOR && layout != TG_COL_MAJOR) return fail(TG_ERR_INVALID_ARGUMENT, "unknown layout %d", int(layout));
+  if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(TG_ERR_INVALID_ARGUMENT, "negative size (batch=%lld m=%lld n=%lld k=%lld)", (long long)batch, (long long)m, (long long)n, (long long)k);
+  if (batch == 0 || m == 0 || n == 0) return TG_OK;
+  if (!c) return fail(TG_ERR_INVALID_ARGUMENT, "C is null");
+  if (k > 0 && (!a || !b)) return fail(TG_ERR_INVALID_ARGUMENT, "A or B is null");
+  if (k >= (int64_t(1) << 31)) return fail(TG_ERR_UNSUPPORTED, "K=%lld exceeds the int32 argmax range", (long long)k);
+  // Leading-dimension checks in the caller's layout.
+  const bool row = layout == TG_ROW_MAJOR;
+  const int64_t need_lda = row ? k : m, need_ldb = row ? n : k, need_ldc = row ? n : m;
+  if (k > 0 && lda < std::max<int64_t>(1, need_lda)) return fail(TG_ERR_DIMENSION_MISMATCH, "lda=%lld < %lld", (long long)lda, (long long)need_lda);
+  if (k > 0 && ldb < std::max<int64_t>(1, need_ldb)) return fail(TG_ERR_DIMENSION_MISMATCH, "ldb=%lld < %lld", (long long)ldb, (long long)need_ldb);
+  if (ldc < std::max<int64_t>(1, need_ldc)) return fail(TG_ERR_DIMENSION_MISMATCH, "ldc=%lld < %lld", (long long)ldc, (long long)need_ldc);
+  if (batch > 1 && (sa < 0 || sb < 0 || sc < 0)) return fail(TG_ERR_INVALID_ARGUMENT, "negative batch stride");
+
+  Problem P;
+  P.batch = batch;
+  if (row) {
+    P.g = tg::GemmArgs{m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc, argmax};
+  } else {  // C^T (N x M, row-major, ldc) = B^T (N x K, ldb) (x) A^T (K x M, lda)
+    P.g = tg::GemmArgs{n, m, k, b, ldb, sb, a, lda, sa, c, ldc, sc, argmax};
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case TG_F32: return dispatch_semiring<float>(semiring, P, st);
+    case TG_F64: return dispatch_semiring<double>(semiring, P, st);
+    case TG_I32: return dispatch_semiring<int32_t>(semiring, P, st);
+    case TG_I64: return dispatch_semiring<int64_t>(semiring, P, st);
+  }
+  return fail(TG_ERR_INVALID_ARGUMENT, "unknown dtype");
+}
+
+// ------------------------------------------------------------- backward
+template <typename T>
+tg_status hist_launch(bool rows_kind, const tg::HistArgs& h, int64_t batch, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int max_optin = 0;
+  cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const size_t bins = rows_kind ? size_t(h.k) * sizeof(T) : size_t(h.k) * 32 * sizeof(T);
+  for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, batch - b0);
+    tg::HistArgs g = h;
+    g.gc = static_cast<const T*>(h.gc) + b0 * h.sc;
+    g.arg = h.arg + b0 * h.sc;
+    if (h.w) g.w = static_cast<const T*>(h.w) + b0 * h.sw;
+    g.out = static_cast<T*>(h.out) + b0 * h.so;
+    if (bins <= size_t(max_optin) && (rows_kind ? h.rows <= 0x7fffffff : (h.cols + 31) / 32 <= 0x7fffffff)) {
+      if (rows_kind) {
+        auto kern = tg::hist_rows_kernel<T>;
+        if (bins > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bins));
+        kern<<<dim3(unsigned(h.rows), unsigned(nb)), 256, bins, st>>>(g);
+      } else {
+        auto kern = tg::hist_cols_kernel<T>;
+        if (bins > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bins));
+        kern<<<dim3(unsigned((h.cols + 31) / 32), unsigned(nb)), 256, bins, st>>>(g);
+      }
+    } else {
+      const int64_t out_rows = rows_kind ? h.rows : h.k, out_cols = rows_kind ? h.k : h.cols;
+      if (!h.accumulate)
+        tg::zero_matrix_kernel<T><<<dim3(1024, unsigned(nb)), 256, 0, st>>>(static_cast<T*>(g.out), out_rows, out_cols, h.ldo, h.so);
+      if (rows_kind) tg::hist_atomic_kernel<T, true><<<dim3(2048, unsigned(nb)), 256, 0, st>>>(g);
+      else tg::hist_atomic_kernel<T, false><<<dim3(2048, unsigned(nb)), 256, 0, st>>>(g);
+    }
+    tg_status s = check_launch("backward launch");
+    if (s != TG_OK) return s;
+  }
+  return TG_OK;
+}
+
+tg_status backward_impl(bool want_a, tg_semiring semiring, tg_dtype dtype, tg_layout layout,
+                        int64_t batch, int64_t m, int64_t n, int64_t k,
+                        const void* grad_c, int64_t ldc, int64_t sc, const int32_t* argmax,
+                        const void* w, int64_t ldw, int64_t sw,
+                        void* grad, int64_t ldg, int64_t sg, int accumulate, void* stream) {
+  g_last_error.clear();
+  if (semiring < TG_MAXPLUS || semiring > TG_MAXMUL) return fail(TG_ERR_INVALID_ARGUMENT, "unknown semiring %d", int(semiring));
+  if (dtype != TG_F32 && dtype != TG_F64) return fail(TG_ERR_UNSUPPORTED, "backward is defined for f32/f64 only");
+  if (layout != TG_ROW_MAJOR && layout != TG_COL_MAJOR) return fail(TG_ERR_INVALID_ARGUMENT, "unknown layout %d", int(layout));
+  if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(TG_ERR_INVALID_ARGUMENT, "negative size");
+  if (batch == 0 || k == 0) return TG_OK;
+  const bool row = layout == TG_ROW_MAJOR;
+  // Output dims in caller layout: grad_A is M x K, grad_B is K x N.
+  const int64_t g_rows = want_a ? m : k, g_cols = want_a ? k : n;
+  if (g_rows == 0 || g_cols == 0) return TG_OK;
+  if (!grad) return fail(TG_ERR_INVALID_ARGUMENT, "gradient output is null");
+  const bool empty_c = (m == 0 || n == 0);
+  if (!empty_c && (!grad_c || !argmax)) return fail(TG_ERR_INVALID_ARGUMENT, "grad_c or argmax is null");
+  if (semiring == TG_MAXMUL && !empty_c && !w) return fail(TG_ERR_INVALID_ARGUMENT, "MaxMul backward needs the partner matrix (%s)", want_a ? "B" : "A");
+  const int64_t need_ldc = row ? n : m;
+  const int64_t need_ldg = row ? g_cols : g_rows;
+  if (!empty_c && ldc < std::max<int64_t>(1, need_ldc)) return fail(TG_ERR_DIMENSION_MISMATCH, "ldc=%lld < %lld", (long long)ldc, (long long)need_ldc);
+  if (ldg < std::max<int64_t>(1, need_ldg)) return fail(TG_ERR_DIMENSION_MISMATCH, "gradient ld=%lld < %lld", (long long)ldg, (long long)need_ldg);
+  if (semiring == TG_MAXMUL && !empty_c) {
+    // partner: B (K x N) for grad_A, A (M x K) for grad_B, in caller layout
+    const int64_t need_ldw = want_a ? (row ? n : k) : (row ? k : m);
+    if (ldw < std::max<int64_t>(1, need_ldw)) return fail(TG_ERR_DIMENSION_MISMATCH, "partner ld=%lld < %lld", (long long)ldw, (long long)need_ldw);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  tg::HistArgs h;
+  // Canonical (row-major) view: row-major grad_A = row histogram, grad_B =
+  // column histogram; column-major swaps the two roles (C^T = B^T (x) A^T).
+  const bool rows_kind = (want_a == row);
+  h.rows = row ? m : n;
+  h.cols = row ? n : m;
+  h.k = k;
+  h.gc = grad_c; h.ldc = ldc; h.sc = sc; h.arg = argmax;
+  h.w = semiring == TG_MAXMUL ? w : nullptr; h.ldw = ldw; h.sw = sw;
+  h.out = grad; h.ldo = ldg; h.so = sg;
+  h.accumulate = accumulate;
+  if (empty_c) {  // nothing scatters; overwrite means zero
+    if (accumulate) return TG_OK;
+    const int64_t orow = rows_kind ? h.rows : k, ocol = rows_kind ? k : h.cols;
+    (void)orow; (void)ocol;
+    if (dtype == TG_F32) tg::zero_matrix_kernel<float><<<dim3(256, unsigned(std::min<int64_t>(batch, 65535))), 256, 0, st>>>(static_cast<float*>(grad), rows_kind ? h.rows : k, rows_kind ? k : h.cols, ldg, sg);
+    else tg::zero_matrix_kernel<double><<<dim3(256, unsigned(std::min<int64_t>(batch, 65535))), 256, 0, st>>>(static_cast<double*>(grad), rows_kind ? h.rows : k, rows_kind ? k : h.cols, ldg, sg);
+    return check_launch("zero_matrix_kernel launch");
+  }
+  return dtype == TG_F32 ? hist_launch<float>(rows_kind, h, batch, st) : hist_launch<double>(rows_kind, h, batch, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tg_version(void) { return "0.2.0-b200"; }
+const char* tg_last_error(void) { return g_last_error.c_str(); }
+
+int tg_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+  return n;
+}
+
+tg_status tg_gemm(tg_semiring semiring, tg_dtype dtype, tg_layout layout, int64_t m, int64_t n, int64_t k,
+                  const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                  int32_t* argmax, void* stream) {
+  return gemm_impl(semiring, dtype, layout, 1, m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, argmax, stream);
+}
+
+tg_status tg_gemm_strided_batched(tg_semiring semiring, tg_dtype dtype, tg_layout layout, int64_t batch,
+                                  int64_t m, int64_t n, int64_t k, const void* a, int64_t lda, int64_t stride_a,
+                                  const void* b, int64_t ldb, int64_t stride_b, void* c, int64_t ldc,
+                                  int64_t stride_c, int32_t* argmax, void* stream) {
+  return gemm_impl(semiring, dtype, layout, batch, m, n, k, a, lda, stride_a, b, ldb, stride_b, c, ldc, stride_c,
+                   argmax, stream);
+}
+
+tg_status tg_backward_a(tg_semiring semiring, tg_dtype dtype, tg_layout layout, int64_t batch, int64_t m, int64_t n,
+                        int64_t k, const void* grad_c, int64_t ldc, int64_t stride_c, const int32_t* argmax,
+                        const void* b, int64_t ldb, int64_t stride_b, void* grad_a, int64_t lda, int64_t stride_a,
+                        int accumulate, void* stream) {
+  return backward_impl(true, semiring, dtype, layout, batch, m, n, k, grad_c, ldc, stride_c, argmax, b, ldb, stride_b,
+                       grad_a, lda, stride_a, accumulate, stream);
+}
+
+tg_status tg_backward_b(tg_semiring semiring, tg_dtype dtype, tg_layout layout, int64_t batch, int64_t m, int64_t n,
+                        int64_t k, const void* grad_c, int64_t ldc, int64_t stride_c, const int32_t* argmax,
+                        const void* a, int64_t lda, int64_t stride_a, void* grad_b, int64_t ldb, int64_t stride_b,
+                        int accumulate, void* stream) {
+  return backward_impl(false, semiring, dtype, layout, batch, m, n, k, grad_c, ldc, stride_c, argmax, a, lda, stride_a,
+                       grad_b, ldb, stride_b, accumulate, stream);
+}
+
+}  // extern "C"
