@@ -1,0 +1,364 @@
+"""Benchmark: tropical ops/s (M*N*K/s) of f32 MaxPlus + argmax at 8192^3 on B200.
+
+Contract (one JSON line on rank 0):
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
+
+* N = 1: BASELINE config 2a -- MaxPlus<f32> with argmax, M = N = K = 8192,
+  A and B i.i.d. standard normal from numpy seed 1 (drawn A then B).
+  A step is one C = A (x) B with argmax over the whole matrix, inputs already
+  in HBM.  A + B = 512 MiB > the 126 MB L2, so no explicit flush is needed.
+* N > 1 (torchrun, one process per GPU, NCCL): weak scaling by row blocks of
+  A -- every rank owns an 8192-row shard of A (M = 8192 * N in total), B
+  (8192 x 8192) is broadcast from rank 0 over NVLink inside every timed step,
+  C and argmax stay sharded (no reduction).  value = all ranks' ops / max time.
+* e2e: the same step through the public API with host buffers -- pinned
+  A and B copied in, tropical_gemm.maxplus_matmul_dlpack run, C and argmax
+  copied back -- timed with CUDA events around everything.
+* roofline: the fast kernel against the FP32 SIMT-pipe roofline
+  (148 SMs x 128 tropical ops / clk, one FADD-lane slot per op).
+* cpu_baseline: the reference's CPU argmax path (its BLIS + scalar 4x4
+  microkernel, restated in oracle/tg_oracle.c) on a bounded row sample.
+* --impl reference: times the reference's CPU implementation (the same
+  restatement, all host threads) on the same config and, as an extra key,
+  the reference's own CUDA kernel built from its sources (oracle/_ref).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tropical-gemm_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+M = N_ = K = 8192
+SEED = 1
+METRIC = "Tropical ops/s (M*N*K/s) f32 MaxPlus+argmax 8192^3 per B200 (weak-scaled row shards for N>1)"
+UNIT = "tropical_ops/s"
+
+
+class ClockSampler:
+    """nvidia-smi sampling (every 200 ms) of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [x for x in sm if x > 0.5 * (mx or max(sm))] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(rows: int, seed: int = SEED):
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((rows, K), dtype=np.float32)
+    b = rng.standard_normal((K, N_), dtype=np.float32)
+    return a, b
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the fast argmax kernel from the committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", "fast_f32_argmax_maxplus_8192.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(rows: int, threads: int):
+    """Reference CPU argmax path (restated) on `rows` rows of the workload."""
+    from oracle import tg_oracle
+    a, b = make_inputs(rows, seed=SEED)
+    t0 = time.perf_counter()
+    tg_oracle.blis_argmax_f32("maxplus", a, b, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return rows * N_ * K / dt, dt
+
+
+def dist_setup(n_gpus: int):
+    if n_gpus > 1 or "RANK" in os.environ:
+        import torch.distributed as dist
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        return dist, rank, world, local
+    torch.cuda.set_device(0)
+    return None, 0, 1, 0
+
+
+def run_engine(args):
+    from tropical_gemm import _native as Nat
+    import tropical_gemm
+
+    dist, rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    a_np, b_np = make_inputs(M, seed=SEED + rank)  # rank r owns rows [8192 r, 8192 (r+1)) of A
+    if rank != 0:
+        b_np = make_inputs(1, seed=SEED)[1]
+    a = torch.from_numpy(a_np).to(dev)
+    b = torch.from_numpy(b_np).to(dev)
+    c = torch.empty((M, N_), device=dev)
+    am = torch.empty((M, N_), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    lib = Nat.lib()
+
+    def gemm():
+        Nat.check(lib.tg_gemm(0, 0, 0, M, N_, K, a.data_ptr(), K, b.data_ptr(), N_, c.data_ptr(), N_,
+                              am.data_ptr(), stream.cuda_stream))
+
+    def step():
+        if dist is not None:
+            dist.broadcast(b, src=0)
+        gemm()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    with ClockSampler(local) as clk:
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            if dist is not None:
+                dist.broadcast(b, src=0)
+            ev[2 * i].record(stream)
+            gemm()
+            ev[2 * i + 1].record(stream)
+        t1.record(stream)
+        barrier()
+    total_ms = t0.elapsed_time(t1)
+    kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)]
+    if dist is not None:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ops_step = float(M) * N_ * K * world
+    value = ops_step * args.steps / (total_ms * 1e-3)
+
+    # e2e through the public API with host buffers (pinned), rank-local
+    a_h = torch.from_numpy(a_np).pin_memory()
+    b_h = torch.from_numpy(b_np).pin_memory()
+    c_h = torch.empty((M * N_,), dtype=torch.float32).pin_memory()
+    am_h = torch.empty((M * N_,), dtype=torch.int32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 5))
+
+    def e2e_step():
+        da = a_h.to(dev, non_blocking=True)
+        db = b_h.to(dev, non_blocking=True)
+        if dist is not None:
+            dist.broadcast(db, src=0)
+        cc, aa = tropical_gemm.maxplus_matmul_dlpack(da, db)
+        c_h.copy_(cc, non_blocking=True)
+        am_h.copy_(aa, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = ops_step * e2e_steps / (e2e_ms * 1e-3)
+
+    if rank == 0:
+        peaks = measured_peaks()
+        clocks = clk.summary()
+        props = torch.cuda.get_device_properties(dev)
+        sm_max = peaks.get("sm_max_mhz") or clocks.get("sm_max_mhz") or 1965.0
+        peak = props.multi_processor_count * 128 * sm_max * 1e6
+        avg_kern_s = statistics.mean(kern_ms) * 1e-3
+        achieved = float(M) * N_ * K / avg_kern_s
+        out = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic: numpy default_rng(seed 1 + rank) standard normal, A then B (BASELINE config 2a)",
+            "config": {"workload": "maxplus_f32_argmax", "m_per_gpu": M, "n": N_, "k": K,
+                       "m_total": M * world, "layout": "row-major",
+                       "b_broadcast": "nccl broadcast from rank 0 inside each step" if world > 1 else "none",
+                       "l2": "inputs (A+B = 512 MiB) exceed the 126 MB L2; no flush"},
+            "roofline": {"bound": "simt", "achieved": achieved / 1e12, "peak": peak / 1e12, "unit": "Tops/s",
+                         "frac": achieved / peak, "traffic": profile_traffic(),
+                         "peak_basis": f"{props.multi_processor_count} SMs x 128 ops/clk x {sm_max:.0f} MHz "
+                                       "(FP32 SIMT pipes; tropical GEMM cannot use tensor cores)",
+                         "frac_at_sampled_clock": (achieved / (props.multi_processor_count * 128 * clocks["sm_mhz"] * 1e6))
+                         if clocks.get("sm_mhz") else None},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * (M * K + K * N_),
+                    "d2h_bytes_per_step": 8 * M * N_, "api": "tropical_gemm.maxplus_matmul_dlpack"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
+        }
+        if world == 1 and not args.no_cpu:
+            rows = args.cpu_rows
+            threads = os.cpu_count() or 1
+            v, dt = cpu_baseline(rows, threads)
+            out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                                   "sample": f"{rows} x {N_} x {K} rows of the same workload, {dt:.1f} s, "
+                                             "reference BLIS argmax path (mc=nc=64,kc=256, 4x4 scalar) restated "
+                                             "in C, OpenMP over column blocks"}
+        print(json.dumps(out), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    rows = args.cpu_rows
+    for _ in range(args.warmup):
+        cpu_baseline(max(8, rows // 8), threads)
+    vals, secs = [], 0.0
+    for _ in range(args.steps):
+        v, dt = cpu_baseline(rows, threads)
+        vals.append(v)
+        secs += dt
+    value = float(np.mean(vals))
+    out = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: numpy default_rng(seed 1) standard normal (BASELINE config 2a), row sample",
+        "config": {"workload": "maxplus_f32_argmax", "m_per_gpu": M, "n": N_, "k": K},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows x {N_} x {K} per step: the reference CPU argmax path "
+                                   "(BLIS + 4x4 scalar microkernel) restated in C (the Rust reference cannot be "
+                                   "built here), all host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    # The reference's own CUDA kernel on this GPU (built from its sources).
+    try:
+        if torch.cuda.is_available():
+            from oracle.ref_gpu import ref_lib, ref_rowmajor
+            if ref_lib() is not None:
+                dev = torch.device("cuda", 0)
+                a_np, b_np = make_inputs(M)
+                a = torch.from_numpy(a_np).to(dev)
+                b = torch.from_numpy(b_np).to(dev)
+                for _ in range(2):
+                    ref_rowmajor("maxplus", a, b, True)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                reps = 3
+                for _ in range(reps):
+                    ref_rowmajor("maxplus", a, b, True)
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / reps
+                out["reference_gpu"] = {"value": float(M) * N_ * K / (ms * 1e-3), "unit": UNIT, "ms_per_launch": ms,
+                                        "kernel": "tropical_maxplus_f32_nn_with_argmax (reference source, nvcc sm_100a)"}
+    except Exception as e:  # the CPU figure above is the arm's value; this key is informational
+        out["reference_gpu"] = {"error": str(e)[:200]}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    p.add_argument("--cpu-rows", type=int, default=64)
+    p.add_argument("--no-cpu", action="store_true")
+    args = p.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_engine(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -9,7 +9,6 @@ from tropical_gemm import _native as N
 from oracle import tg_oracle as O
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libref_gpu.so")
 SEMIS = ("maxplus", "minplus", "maxmul")
 NP2T = {np.float32: torch.float32, np.float64: torch.float64, np.int32: torch.int32, np.int64: torch.int64}
 
@@ -57,34 +56,4 @@ def oracle(semi, a, b, with_argmax=True):
     return O.gemm(semi, a, b, with_argmax)
 
 
-_ref = None
-
-
-def ref_lib():
-    """The reference's own CUDA kernels (built from its sources into oracle/_ref)."""
-    global _ref
-    if _ref is None:
-        if not os.path.exists(REF_LIB):
-            return None
-        L = ctypes.CDLL(REF_LIB)
-        i, vp = ctypes.c_int, ctypes.c_void_p
-        L.ref_gemm.argtypes = [i, i, i, i, i, i, vp, vp, vp, vp, vp]
-        L.ref_gemm_batched_argmax_f32.argtypes = [i, i, i, i, i, vp, vp, vp, vp, i, i, i, vp]
-        L.ref_backward.argtypes = [i, i, vp, vp, vp, i, i, i, vp]
-        _ref = L
-    return _ref
-
-
-def ref_rowmajor(semi, ta: torch.Tensor, tb: torch.Tensor, with_argmax=True):
-    """Reference kernel on row-major device tensors via its swap convention
-    (crates/tropical-gemm-cuda/src/kernels.rs:416-430): C^T = B^T (x) A^T."""
-    L = ref_lib()
-    m, k = ta.shape
-    n = tb.shape[1]
-    c = torch.empty((m, n), dtype=ta.dtype, device=ta.device)
-    am = torch.empty((m, n), dtype=torch.int32, device=ta.device) if with_argmax else None
-    rc = L.ref_gemm(N.SEMIRINGS[semi], N.DTYPES[ta.dtype], int(with_argmax), n, m, k, tb.data_ptr(), ta.data_ptr(),
-                    c.data_ptr(), am.data_ptr() if am is not None else None,
-                    torch.cuda.current_stream().cuda_stream)
-    assert rc == 0
-    return c, am
+from oracle.ref_gpu import ref_lib, ref_rowmajor  # noqa: E402,F401

@@ -331,3 +331,9 @@ tg_status tg_backward_b(tg_semiring semiring, tg_dtype dtype, tg_layout layout, 
 }
 
 }  // extern "C"
+
+#ifdef TG_PHASE_TIMING
+extern "C" int tg_debug_phase_ts(long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, tg::tg_phase_ts, sizeof(long long) * n);
+}
+#endif

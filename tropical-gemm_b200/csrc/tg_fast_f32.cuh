@@ -30,6 +30,13 @@
 
 namespace tg {
 
+#ifdef TG_PHASE_TIMING
+__device__ long long tg_phase_ts[8192 * 6];
+#define TG_PHASE(i) do { if (threadIdx.x == 0 && blockIdx.z == 0) { unsigned bid = blockIdx.x + gridDim.x * blockIdx.y; if (bid < 8192) tg_phase_ts[bid * 6 + (i)] = clock64(); } } while (0)
+#else
+#define TG_PHASE(i) do {} while (0)
+#endif
+
 constexpr int kFBM = 128, kFBN = 128, kFBK = 32, kFThreads = 256, kFStages = 3;
 constexpr int kFApitch = kFBK + 4;                 // floats per staged A row
 constexpr int kFAStage = kFBM * kFApitch;          // floats
@@ -39,7 +46,12 @@ constexpr int kFMaxChunks = 1024;
 constexpr uint16_t kNoChunk = 0xFFFF;
 constexpr uint16_t kResolved = 0xFFFE;
 constexpr size_t kFSmemValues = size_t(kFStages) * kFStageFloats * 4;
-constexpr size_t kFSmemArgmax = kFSmemValues + 2 * size_t(kFBM * kFBN) * 2 + (kFMaxChunks + 1) * 4;
+// argmax extras: chunk ids (u16) and the bucketed output list (u16) per CTA
+// output, bucket offsets, and a resolved-bit per output.  After bucketing,
+// the third pipeline stage plus the chunk-id array (contiguous, >= 64 KiB)
+// hold the final values of all 16384 outputs for the re-stream scan.
+constexpr size_t kFSmemArgmax = kFSmemValues + 2 * size_t(kFBM * kFBN) * 2 + (kFMaxChunks + 1) * 4 + kFBM * kFBN / 8;
+static_assert(size_t(kFStageFloats) * 4 + size_t(kFBM * kFBN) * 2 >= size_t(kFBM * kFBN) * 4, "value cache does not fit");
 
 template <int S> struct FastOps;
 template <> struct FastOps<kMaxPlus> {
@@ -98,39 +110,86 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" :: "n"(N));
 }
 
-// Stage k-tile `kt` of the CTA's A rows [m0, m0+128) and B cols [n0, n0+128).
-// Out-of-range elements are zero-filled (their products are never used or
-// are neutralised by fix_k_tail).
-__device__ __forceinline__ void fast_load_tile(float* stage, const float* __restrict__ A, const float* __restrict__ B,
-                                               const GemmArgs& p, int64_t m0, int64_t n0, int64_t kt, int tid) {
-  const int64_t k0 = kt * kFBK;
-  float* As = stage;
-  float* Bs = stage + kFAStage;
+// Per-thread staging of k-tiles into one pipeline stage, with every address
+// term that does not depend on the tile precomputed once per CTA.
+//  A: 128 rows x 32 k as 16-byte cp.async; thread t copies rows
+//     (t>>3) + 32e, e = 0..3, at k offset 4*(t&7).
+//  B: 32 k x 128 n as 4-byte cp.async into the k-pair-interleaved layout;
+//     thread t copies column t&127 for rows (t>>7) + 2e, e = 0..15, so its
+//     shared-memory destinations are 1 KiB apart and its sources 2*ldb apart.
+// Out-of-range rows/columns are zero-filled (src-size 0) and never stored;
+// the k tail of the last tile is fixed up by fix_k_tail.
+struct TileLoader {
+  const float* a_src;   // A + (m0 + (t>>3)) * lda + 4*(t&7)
+  const float* b_src;   // B + (t>>7) * ldb + n0 + (t&127)
+  int64_t a_step;       // 32 * lda
+  int64_t b_step;       // 2 * ldb
+  int64_t k;
+  uint32_t a_dst, b_dst;
+  int a_kq, b_kpar;
+  uint32_t a_rowmask;   // bit e: row (t>>3) + 32e exists
+  bool b_colok;
+
+  __device__ __forceinline__ TileLoader(const float* A, const float* B, const GemmArgs& p, int64_t m0, int64_t n0,
+                                        int tid, const float* smem_base) {
+    const int ra = tid >> 3;
+    a_kq = (tid & 7) * 4;
+    a_step = 32 * p.lda;
+    a_rowmask = 0;
 #pragma unroll
-  for (int e = 0; e < (kFBM * kFBK / 4) / kFThreads; ++e) {  // 4 x 16B per thread
-    int q = tid + e * kFThreads;
-    int row = q >> 3, kq = (q & 7) * 4;
-    int64_t gr = m0 + row, gk = k0 + kq;
-    int bytes = 0;
-    const float* src = A;
-    if (gr < p.m && gk < p.k) {
-      int64_t rem = p.k - gk;
-      bytes = rem >= 4 ? 16 : int(rem) * 4;
-      src = A + gr * p.lda + gk;
+    for (int e = 0; e < 4; ++e)
+      if (m0 + ra + 32 * e < p.m) a_rowmask |= 1u << e;
+    a_src = (m0 + ra < p.m) ? A + (m0 + ra) * p.lda + a_kq : A;
+    b_kpar = tid >> 7;
+    const int nn = tid & 127;
+    b_colok = (n0 + nn) < p.n;
+    b_step = 2 * p.ldb;
+    b_src = b_colok ? B + int64_t(b_kpar) * p.ldb + n0 + nn : B;
+    k = p.k;
+    a_dst = smem_u32(smem_base) + uint32_t((ra * kFApitch + a_kq) * 4);
+    b_dst = smem_u32(smem_base + kFAStage) + uint32_t((nn * 2 + b_kpar) * 4);
+  }
+
+  __device__ __forceinline__ void load(int stage, int64_t kt) const {
+    const uint32_t soff = uint32_t(stage) * uint32_t(kFStageFloats * 4);
+    const int64_t k0 = kt * kFBK;
+    const bool interior = k0 + kFBK <= k;
+    // A
+    {
+      const float* src = a_src + k0;
+      int bytes = 16;
+      if (!interior) {
+        const int64_t rem = k - (k0 + a_kq);
+        bytes = rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = (a_rowmask >> e) & 1u;
+        cp_async16(a_dst + soff + uint32_t(e * 32 * kFApitch * 4), ok && bytes ? src : a_src, ok ? bytes : 0);
+        src += a_step;
+      }
     }
-    cp_async16(smem_u32(As + row * kFApitch + kq), src, bytes);
-  }
+    // B
+    {
+      const float* src = b_src + k0 * (b_step >> 1);
+      if (interior) {
+        const int bytes = b_colok ? 4 : 0;
 #pragma unroll
-  for (int e = 0; e < (kFBK * kFBN) / kFThreads; ++e) {      // 16 x 4B per thread
-    int lin = tid + e * kFThreads;
-    int kk = lin >> 7, nn = lin & 127;
-    int64_t gk = k0 + kk, gc = n0 + nn;
-    int bytes = 0;
-    const float* src = B;
-    if (gk < p.k && gc < p.n) { bytes = 4; src = B + gk * p.ldb + gc; }
-    cp_async4(smem_u32(Bs + ((kk >> 1) * kFBN + nn) * 2 + (kk & 1)), src, bytes);
+        for (int e = 0; e < 16; ++e) {
+          cp_async4(b_dst + soff + uint32_t(e * kFBN * 2 * 4), src, bytes);
+          src += b_colok ? b_step : 0;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const bool ok = b_colok && (k0 + b_kpar + 2 * e < k);
+          cp_async4(b_dst + soff + uint32_t(e * kFBN * 2 * 4), ok ? src : b_src, ok ? 4 : 0);
+          src += b_colok ? b_step : 0;
+        }
+      }
+    }
   }
-}
+};
 
 // Semiring zero into the A columns k >= K of the last (partial) k-tile, so
 // padded k-pairs never produce a winning product.
@@ -164,6 +223,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
   const int64_t ktiles = (p.k + kFBK - 1) / kFBK;
   const int kvalid_last = int(p.k - (ktiles - 1) * kFBK);
 
+  const TileLoader ldr(A, B, p, m0, n0, tid, smem);
   uint16_t* cid = reinterpret_cast<uint16_t*>(smem + kFStages * kFStageFloats);
   if (ARGMAX) {
     for (int i = tid; i < kFBM * kFBN; i += kFThreads) cid[i] = kNoChunk;
@@ -180,9 +240,10 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     }
 
   // ------------------------------------------------------------ main loop
+  TG_PHASE(0);
 #pragma unroll
   for (int s = 0; s < kFStages - 1; ++s) {
-    if (s < ktiles) fast_load_tile(smem + s * kFStageFloats, A, B, p, m0, n0, s, tid);
+    if (s < ktiles) ldr.load(s, s);
     cp_async_commit();
   }
   for (int64_t t = 0; t < ktiles; ++t) {
@@ -195,7 +256,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     }
     {
       int64_t nt = t + kFStages - 1;
-      if (nt < ktiles) fast_load_tile(smem + (nt % kFStages) * kFStageFloats, A, B, p, m0, n0, nt, tid);
+      if (nt < ktiles) ldr.load(int(nt % kFStages), nt);
       cp_async_commit();
     }
     const float* Ap = stage + (wm * 32 + lm) * kFApitch;
@@ -244,6 +305,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
   cp_async_wait<0>();
 
   // ------------------------------------------------------------ epilogue
+  TG_PHASE(1);
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const int lr = wm * 32 + r * 4 + lm;
@@ -269,6 +331,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
 
   // -------------------------------------------- argmax: bucket by chunk
   __syncthreads();
+  TG_PHASE(2);
   uint16_t* list = cid + kFBM * kFBN;
   int* off = reinterpret_cast<int*>(list + kFBM * kFBN);   // kFMaxChunks + 1
   const int nchunks = int((ktiles + tiles_per_chunk - 1) / tiles_per_chunk);
@@ -294,10 +357,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     }
   }
   __syncthreads();
-  // Scatter: reuse counts as cursors via a second pass with atomics on a
-  // copy kept in the scan results (off[c] is the start; use atomicAdd on a
-  // running cursor stored in the (now free) first stage buffer).
-  int* cursor = reinterpret_cast<int*>(smem);   // stage 0 is idle here
+  // Scatter into buckets; running cursors live in the idle stage-0 buffer.
+  int* cursor = reinterpret_cast<int*>(smem);
   for (int i = tid; i < nchunks; i += kFThreads) cursor[i] = off[i];
   __syncthreads();
   for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
@@ -305,16 +366,26 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     if (ch != kNoChunk) list[atomicAdd(&cursor[ch], 1)] = uint16_t(i);
   }
   __syncthreads();
+  // Chunk ids are no longer needed: cache every output's final value in
+  // shared memory (stage 2 + chunk-id area) and clear the resolved bits.
+  float* vcache = smem + 2 * kFStageFloats;
+  uint32_t* resolved = reinterpret_cast<uint32_t*>(off + kFMaxChunks + 1);
+  for (int i = tid; i < kFBM * kFBN / 32; i += kFThreads) resolved[i] = 0u;
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      vcache[(wm * 32 + r * 4 + lm) * kFBN + wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)] = acc[r][c];
+  __syncthreads();
 
   // ---------------------------- argmax: re-stream owned chunks and scan
+  TG_PHASE(3);
   // Sequence of k-tiles to revisit: all tiles of every chunk that owns at
-  // least one output, in ascending k.
+  // least one output, in ascending k; double-buffered in stages 0 and 1.
   auto next_owned = [&](int c) {
     while (c < nchunks && off[c + 1] == off[c]) ++c;
     return c;
   };
-  int ld_chunk = next_owned(0);
-  int64_t ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
   auto advance = [&](int& ch, int64_t& tl) {
     ++tl;
     if (tl >= int64_t(ch + 1) * tiles_per_chunk || tl >= ktiles) {
@@ -322,27 +393,24 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
       tl = int64_t(ch) * tiles_per_chunk;
     }
   };
-  int64_t issued = 0;
-#pragma unroll
-  for (int s = 0; s < kFStages - 1; ++s) {
-    if (ld_chunk < nchunks) {
-      fast_load_tile(smem + (issued % kFStages) * kFStageFloats, A, B, p, m0, n0, ld_tile, tid);
-      advance(ld_chunk, ld_tile);
-    }
-    ++issued;
-    cp_async_commit();
+  int ld_chunk = next_owned(0);
+  int64_t ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
+  int cur_chunk = ld_chunk;
+  int64_t cur_tile = ld_tile;
+  if (ld_chunk < nchunks) {
+    ldr.load(0, ld_tile);
+    advance(ld_chunk, ld_tile);
   }
-  int cur_chunk = next_owned(0);
-  int64_t cur_tile = int64_t(cur_chunk) * tiles_per_chunk;
+  cp_async_commit();
+  const int grp = tid >> 3, sub = tid & 7;
   for (int64_t it = 0; cur_chunk < nchunks; ++it) {
-    cp_async_wait<kFStages - 2>();
+    cp_async_wait<0>();
     __syncthreads();
-    float* stage = smem + (it % kFStages) * kFStageFloats;
+    const float* stage = smem + (it & 1) * kFStageFloats;
     if (ld_chunk < nchunks) {
-      fast_load_tile(smem + (issued % kFStages) * kFStageFloats, A, B, p, m0, n0, ld_tile, tid);
+      ldr.load(int((it + 1) & 1), ld_tile);
       advance(ld_chunk, ld_tile);
     }
-    ++issued;
     cp_async_commit();
 
     const float* As = stage;
@@ -350,25 +418,45 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     const int64_t k0 = cur_tile * kFBK;
     const int kcount = int((p.k - k0) < kFBK ? (p.k - k0) : kFBK);
     const int beg = off[cur_chunk], end = off[cur_chunk + 1];
-    for (int e = beg + tid; e < end; e += kFThreads) {
-      const int o = list[e];
-      if (cid[o] == kResolved) continue;
+    // 32 groups of 8 lanes; lane `sub` of a group tests k = 4*sub .. 4*sub+3
+    // of this tile for the group's output, then the group takes the lowest
+    // matching k.  The loop trip count is block-uniform, so every lane
+    // reaches the shuffles.
+    for (int e0 = beg; e0 < end; e0 += kFThreads / 8) {
+      const int e = e0 + grp;
+      int o = 0;
+      bool active = e < end;
+      if (active) {
+        o = list[e];
+        active = !((resolved[o >> 5] >> (o & 31)) & 1u);
+      }
       const int lr = o >> 7, lc = o & 127;
-      const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
-      const float v = C[gofs];
-      for (int kk = 0; kk < kcount; ++kk) {
-        const float prod = Op::mul(As[lr * kFApitch + kk], Bs[((kk >> 1) * kFBN + lc) * 2 + (kk & 1)]);
-        if (prod == v) {
-          C[gofs] = prod;
-          IDX[gofs] = int32_t(k0 + kk);
-          cid[o] = kResolved;
-          break;
-        }
+      unsigned cand = 0xFFFFFFFFu;
+      float cp = 0.f;
+      if (active) {
+        const float v = vcache[o];
+        const float4 av = *reinterpret_cast<const float4*>(As + lr * kFApitch + 4 * sub);
+        const float2 b01 = *reinterpret_cast<const float2*>(Bs + ((2 * sub) * kFBN + lc) * 2);
+        const float2 b23 = *reinterpret_cast<const float2*>(Bs + ((2 * sub + 1) * kFBN + lc) * 2);
+        const float pr[4] = {Op::mul(av.x, b01.x), Op::mul(av.y, b01.y), Op::mul(av.z, b23.x), Op::mul(av.w, b23.y)};
+#pragma unroll
+        for (int i = 3; i >= 0; --i)
+          if (4 * sub + i < kcount && pr[i] == v) { cand = unsigned(4 * sub + i); cp = pr[i]; }
+      }
+      unsigned best = cand;
+#pragma unroll
+      for (int d = 1; d < 8; d <<= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, d));
+      if (active && best != 0xFFFFFFFFu && cand == best) {
+        const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
+        C[gofs] = cp;
+        IDX[gofs] = int32_t(k0 + best);
+        atomicOr(&resolved[o >> 5], 1u << (o & 31));
       }
     }
     advance(cur_chunk, cur_tile);
   }
   cp_async_wait<0>();
+  TG_PHASE(4);
 }
 
 }  // namespace tg
