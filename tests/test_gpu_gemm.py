@@ -202,3 +202,27 @@ def test_large_square_vs_oracle_sampled_rows():
     rows = rng.choice(m, 64, replace=False)
     c0, am0 = oracle("maxplus", a[rows], b)
     assert same_bits(c[rows], c0) and np.array_equal(am[rows], am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("pattern", ["increasing", "decreasing", "plateau"])
+def test_argmax_improvement_patterns(semi, pattern):
+    """Running values that improve in every k-chunk, only in the first one,
+    or tie on a long plateau: the chunk bookkeeping must give the reference's
+    first-k winner in all of them."""
+    m, k, n = 256, 1500, 256
+    kk = np.arange(k, dtype=np.float32) * 0.01
+    if semi == "minplus":
+        kk = -kk
+    if pattern == "increasing":
+        a = np.tile(kk, (m, 1)) + 1.0
+    elif pattern == "decreasing":
+        a = np.tile(-kk, (m, 1)) + 1.0
+    else:
+        a = np.ones((m, k), np.float32)
+        a[:, 700:900] = 2.0 if semi != "minplus" else 0.5
+    a = a.astype(np.float32)
+    b = np.ones((k, n), np.float32)
+    c, am = engine(semi, a, b)
+    c0, am0 = oracle(semi, a, b)
+    assert same_bits(c, c0) and np.array_equal(am, am0)

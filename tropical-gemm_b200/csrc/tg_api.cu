@@ -68,6 +68,8 @@ bool fast_f32_ok(const Problem& P) {
   if (g.lda % 4 != 0) return false;
   if (P.batch > 1 && g.sa % 4 != 0) return false;
   if (g.k >= (int64_t(1) << 31)) return false;
+  // argmax: the re-stream ring holds whole chunks of <= 4 k-tiles (1024 chunks)
+  if (g.argmax && (g.k + tg::kFBK - 1) / tg::kFBK > int64_t(4) * tg::kFMaxChunks) return false;
   return true;
 }
 
@@ -85,6 +87,8 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st) {
   }
   const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
   int tpc = 2;
+  const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
+                     (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
   while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
   const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;
   const int64_t gy = (P.g.n + tg::kFBN - 1) / tg::kFBN;
@@ -96,7 +100,7 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st) {
     g.b = static_cast<const float*>(g.b) + b0 * g.sb;
     g.c = static_cast<float*>(g.c) + b0 * g.sc;
     if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
-    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc);
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec);
     tg_status s = check_launch("fast_f32_kernel launch");
     if (s != TG_OK) return s;
   }

@@ -43,15 +43,22 @@ constexpr int kFAStage = kFBM * kFApitch;          // floats
 constexpr int kFBStage = kFBK * kFBN;              // floats
 constexpr int kFStageFloats = kFAStage + kFBStage;
 constexpr int kFMaxChunks = 1024;
-constexpr uint16_t kNoChunk = 0xFFFF;
-constexpr uint16_t kResolved = 0xFFFE;
+constexpr uint16_t kNoChunk = 0xFFFF;              // output never beat the semiring zero
 constexpr size_t kFSmemValues = size_t(kFStages) * kFStageFloats * 4;
-// argmax extras: chunk ids (u16) and the bucketed output list (u16) per CTA
-// output, bucket offsets, and a resolved-bit per output.  After bucketing,
-// the third pipeline stage plus the chunk-id array (contiguous, >= 64 KiB)
-// hold the final values of all 16384 outputs for the re-stream scan.
-constexpr size_t kFSmemArgmax = kFSmemValues + 2 * size_t(kFBM * kFBN) * 2 + (kFMaxChunks + 1) * 4 + kFBM * kFBN / 8;
-static_assert(size_t(kFStageFloats) * 4 + size_t(kFBM * kFBN) * 2 >= size_t(kFBM * kFBN) * 4, "value cache does not fit");
+// Argmax kernel shared-memory map.  During the k loop: the three pipeline
+// stages and one chunk id (u16) per CTA output.  After the outputs are
+// bucketed by chunk, kRStages ring slots (overlaying stages and chunk ids)
+// re-stream the owned chunks; the bucketed list and offsets sit above.
+constexpr int kRStages = 5;
+constexpr int kRBpitch = kFBN + 4;                         // padded B rows: column reads spread over banks
+constexpr int kRStageFloats = kFAStage + kFBK * kRBpitch;  // one ring slot
+constexpr size_t kOffCid = kFSmemValues;
+constexpr size_t kOffList = size_t(kRStages) * kRStageFloats * 4;
+constexpr size_t kOffOff = kOffList + size_t(kFBM * kFBN) * 2;
+constexpr size_t kFSmemArgmax = kOffOff + size_t(kFMaxChunks + 1) * 4;
+static_assert(kOffCid + size_t(kFBM * kFBN) * 2 <= kOffList, "chunk ids overlap the list");
+static_assert(kFSmemArgmax <= 227 * 1024, "argmax kernel exceeds shared memory");
+static_assert((kRStageFloats * 4) % 16 == 0 && (kRBpitch * 4) % 16 == 0, "ring alignment");
 
 template <int S> struct FastOps;
 template <> struct FastOps<kMaxPlus> {
@@ -95,6 +102,8 @@ template <> struct FastOps<kMaxMul> {
   static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
   static __device__ __forceinline__ bool better(float p, float acc) { return p > acc; }
 };
+
+__device__ __forceinline__ int64_t i64min(int64_t a, int64_t b) { return a < b ? a : b; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -152,9 +161,13 @@ struct TileLoader {
 
   __device__ __forceinline__ void load(int stage, int64_t kt) const {
     const uint32_t soff = uint32_t(stage) * uint32_t(kFStageFloats * 4);
+    load_a_at(soff, kt);
+    load_b(soff, kt);
+  }
+
+  __device__ __forceinline__ void load_a_at(uint32_t soff, int64_t kt) const {
     const int64_t k0 = kt * kFBK;
     const bool interior = k0 + kFBK <= k;
-    // A
     {
       const float* src = a_src + k0;
       int bytes = 16;
@@ -169,7 +182,11 @@ struct TileLoader {
         src += a_step;
       }
     }
-    // B
+  }
+
+  __device__ __forceinline__ void load_b(uint32_t soff, int64_t kt) const {
+    const int64_t k0 = kt * kFBK;
+    const bool interior = k0 + kFBK <= k;
     {
       const float* src = b_src + k0 * (b_step >> 1);
       if (interior) {
@@ -191,6 +208,54 @@ struct TileLoader {
   }
 };
 
+// Re-stream staging into a ring slot: A exactly as in the k loop, B in its
+// natural [k][n] layout with padded rows (the scan reads single columns, so
+// the k-pair interleave is not needed).  16-byte copies when B rows are
+// 16-byte aligned, 4-byte copies otherwise.
+struct RestreamLoader {
+  const TileLoader* main;
+  const float* B;
+  int64_t n0, kdim, ndim, ldb;
+  int tid;
+  bool b_vec;
+  uint32_t base;
+  __device__ __forceinline__ RestreamLoader(const TileLoader* ml, const float* B_, const GemmArgs& p, int64_t n0_,
+                                            int tid_, const float* smem_base, bool vec)
+      : main(ml), B(B_), n0(n0_), kdim(p.k), ndim(p.n), ldb(p.ldb), tid(tid_), b_vec(vec),
+        base(smem_u32(smem_base)) {}
+  __device__ __forceinline__ void load(int slot, int64_t kt) const {
+    const uint32_t soff = uint32_t(slot) * uint32_t(kRStageFloats * 4);
+    main->load_a_at(soff, kt);
+    const uint32_t bbase = base + soff + uint32_t(kFAStage * 4);
+    const int64_t k0 = kt * kFBK;
+    if (b_vec) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = tid + e * kFThreads;
+        const int kk = q >> 5, c4 = (q & 31) * 4;
+        const int64_t gk = k0 + kk, gc = n0 + c4;
+        int bytes = 0;
+        const float* src = B;
+        if (gk < kdim && gc < ndim) {
+          const int64_t rem = ndim - gc;
+          bytes = rem >= 4 ? 16 : int(rem) * 4;
+          src = B + gk * ldb + gc;
+        }
+        cp_async16(bbase + uint32_t((kk * kRBpitch + c4) * 4), src, bytes);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int q = tid + e * kFThreads;
+        const int kk = q >> 7, c = q & 127;
+        const int64_t gk = k0 + kk, gc = n0 + c;
+        const bool ok = gk < kdim && gc < ndim;
+        cp_async4(bbase + uint32_t((kk * kRBpitch + c) * 4), ok ? B + gk * ldb + gc : B, ok ? 4 : 0);
+      }
+    }
+  }
+};
+
 // Semiring zero into the A columns k >= K of the last (partial) k-tile, so
 // padded k-pairs never produce a winning product.
 template <int S>
@@ -205,9 +270,10 @@ __device__ __forceinline__ void fix_k_tail(float* stage, int kvalid, int tid) {
 
 template <int S, bool ARGMAX>
 __global__ void __launch_bounds__(kFThreads, 1)
-fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
+fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
   using Op = FastOps<S>;
   extern __shared__ __align__(16) float smem[];
+  unsigned char* sbytes = reinterpret_cast<unsigned char*>(smem);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int lm = lane >> 3, ln = lane & 7;
@@ -224,7 +290,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
   const int kvalid_last = int(p.k - (ktiles - 1) * kFBK);
 
   const TileLoader ldr(A, B, p, m0, n0, tid, smem);
-  uint16_t* cid = reinterpret_cast<uint16_t*>(smem + kFStages * kFStageFloats);
+  uint16_t* cid = reinterpret_cast<uint16_t*>(sbytes + kOffCid);
   if (ARGMAX) {
     for (int i = tid; i < kFBM * kFBN; i += kFThreads) cid[i] = kNoChunk;
   }
@@ -288,16 +354,14 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
       }
     }
     if (ARGMAX && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
+      // chunk boundary: remember the chunk of each output's latest strict improvement
       const uint16_t chunk = uint16_t(t / tiles_per_chunk);
 #pragma unroll
       for (int r = 0; r < 8; ++r)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          if (Op::better(acc[r][c], snap[r][c])) {
-            const int lr = wm * 32 + r * 4 + lm;
-            const int lc = wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1);
-            cid[lr * kFBN + lc] = chunk;
-          }
+          if (Op::better(acc[r][c], snap[r][c]))
+            cid[(wm * 32 + r * 4 + lm) * kFBN + wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)] = chunk;
           snap[r][c] = acc[r][c];
         }
     }
@@ -318,13 +382,12 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
         if (ARGMAX) cid[lr * kFBN + lc] = kNoChunk;   // padding: never resolved
         continue;
       }
-      float v = acc[r][c];
-      if (ARGMAX) {
-        const uint16_t ch = cid[lr * kFBN + lc];
-        if (ch == kNoChunk) { v = Op::zero(); IDX[gr * p.ldc + gc] = 0; }
-        else IDX[gr * p.ldc + gc] = int32_t(int64_t(ch) * tiles_per_chunk * kFBK);
+      if (!ARGMAX) {
+        C[gr * p.ldc + gc] = acc[r][c];
+      } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
+        C[gr * p.ldc + gc] = Op::zero();
+        IDX[gr * p.ldc + gc] = 0;
       }
-      C[gr * p.ldc + gc] = v;
     }
   }
   if (!ARGMAX) return;
@@ -332,8 +395,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
   // -------------------------------------------- argmax: bucket by chunk
   __syncthreads();
   TG_PHASE(2);
-  uint16_t* list = cid + kFBM * kFBN;
-  int* off = reinterpret_cast<int*>(list + kFBM * kFBN);   // kFMaxChunks + 1
+  uint16_t* list = reinterpret_cast<uint16_t*>(sbytes + kOffList);
+  int* off = reinterpret_cast<int*>(sbytes + kOffOff);
   const int nchunks = int((ktiles + tiles_per_chunk - 1) / tiles_per_chunk);
   for (int i = tid; i <= nchunks; i += kFThreads) off[i] = 0;
   __syncthreads();
@@ -342,7 +405,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     if (ch != kNoChunk) atomicAdd(&off[ch + 1], 1);
   }
   __syncthreads();
-  if (warp == 0) {  // inclusive scan of counts -> bucket starts (off[c]..off[c+1])
+  if (warp == 0) {  // inclusive scan of counts: bucket c is list[off[c], off[c+1])
     int carry = 0;
     for (int base = 1; base <= nchunks; base += 32) {
       int i = base + lane;
@@ -357,8 +420,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     }
   }
   __syncthreads();
-  // Scatter into buckets; running cursors live in the idle stage-0 buffer.
-  int* cursor = reinterpret_cast<int*>(smem);
+  int* cursor = reinterpret_cast<int*>(smem);   // stage 0 is idle here
   for (int i = tid; i < nchunks; i += kFThreads) cursor[i] = off[i];
   __syncthreads();
   for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
@@ -366,94 +428,108 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk) {
     if (ch != kNoChunk) list[atomicAdd(&cursor[ch], 1)] = uint16_t(i);
   }
   __syncthreads();
-  // Chunk ids are no longer needed: cache every output's final value in
-  // shared memory (stage 2 + chunk-id area) and clear the resolved bits.
-  float* vcache = smem + 2 * kFStageFloats;
-  uint32_t* resolved = reinterpret_cast<uint32_t*>(off + kFMaxChunks + 1);
-  for (int i = tid; i < kFBM * kFBN / 32; i += kFThreads) resolved[i] = 0u;
-#pragma unroll
-  for (int r = 0; r < 8; ++r)
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      vcache[(wm * 32 + r * 4 + lm) * kFBN + wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)] = acc[r][c];
-  __syncthreads();
 
-  // ---------------------------- argmax: re-stream owned chunks and scan
+  // ---------------------- argmax: re-stream the chunks that own outputs
+  // Every output of chunk c had its last strict improvement in c, so its
+  // final value is the max (min) of its products over c, and its reference
+  // index is the first k of c whose product equals that value.  Tiles of the
+  // owned chunks stream through a kRStages-deep ring (the chunk ids are dead
+  // now); a chunk is scanned once all its tiles have landed.
   TG_PHASE(3);
-  // Sequence of k-tiles to revisit: all tiles of every chunk that owns at
-  // least one output, in ascending k; double-buffered in stages 0 and 1.
+  const RestreamLoader rl(&ldr, B, p, n0, tid, smem, b_vec != 0);
   auto next_owned = [&](int c) {
     while (c < nchunks && off[c + 1] == off[c]) ++c;
     return c;
   };
-  auto advance = [&](int& ch, int64_t& tl) {
-    ++tl;
-    if (tl >= int64_t(ch + 1) * tiles_per_chunk || tl >= ktiles) {
-      ch = next_owned(ch + 1);
-      tl = int64_t(ch) * tiles_per_chunk;
-    }
-  };
   int ld_chunk = next_owned(0);
   int64_t ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
-  int cur_chunk = ld_chunk;
-  int64_t cur_tile = ld_tile;
-  if (ld_chunk < nchunks) {
-    ldr.load(0, ld_tile);
-    advance(ld_chunk, ld_tile);
-  }
-  cp_async_commit();
-  const int grp = tid >> 3, sub = tid & 7;
-  for (int64_t it = 0; cur_chunk < nchunks; ++it) {
-    cp_async_wait<0>();
-    __syncthreads();
-    const float* stage = smem + (it & 1) * kFStageFloats;
-    if (ld_chunk < nchunks) {
-      ldr.load(int((it + 1) & 1), ld_tile);
-      advance(ld_chunk, ld_tile);
-    }
-    cp_async_commit();
-
-    const float* As = stage;
-    const float* Bs = stage + kFAStage;
-    const int64_t k0 = cur_tile * kFBK;
-    const int kcount = int((p.k - k0) < kFBK ? (p.k - k0) : kFBK);
-    const int beg = off[cur_chunk], end = off[cur_chunk + 1];
-    // 32 groups of 8 lanes; lane `sub` of a group tests k = 4*sub .. 4*sub+3
-    // of this tile for the group's output, then the group takes the lowest
-    // matching k.  The loop trip count is block-uniform, so every lane
-    // reaches the shuffles.
-    for (int e0 = beg; e0 < end; e0 += kFThreads / 8) {
-      const int e = e0 + grp;
-      int o = 0;
-      bool active = e < end;
-      if (active) {
-        o = list[e];
-        active = !((resolved[o >> 5] >> (o & 31)) & 1u);
+  int64_t issued = 0;
+  auto issue_until = [&](int64_t limit) {
+    while (ld_chunk < nchunks && issued < limit) {
+      rl.load(int(issued % kRStages), ld_tile);
+      cp_async_commit();
+      ++issued;
+      ++ld_tile;
+      if (ld_tile >= int64_t(ld_chunk + 1) * tiles_per_chunk || ld_tile >= ktiles) {
+        ld_chunk = next_owned(ld_chunk + 1);
+        ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
       }
+    }
+  };
+  issue_until(kRStages);
+  int64_t seq0 = 0;   // ring sequence number of the current chunk's first tile
+  const int grp = tid >> 2, sub = tid & 3;
+  for (int c = next_owned(0); c < nchunks; c = next_owned(c + 1)) {
+    const int64_t t0 = int64_t(c) * tiles_per_chunk;
+    const int nt = int(i64min(tiles_per_chunk, ktiles - t0));
+    const int64_t need = seq0 + nt;
+    if (issued < need) {   // chunks longer than two tiles: make room, then issue the rest
+      __syncthreads();
+      issue_until(need);
+    }
+    const int64_t pending = issued - need;   // groups allowed to stay in flight
+    if (pending >= 4) cp_async_wait<4>();
+    else if (pending == 3) cp_async_wait<3>();
+    else if (pending == 2) cp_async_wait<2>();
+    else if (pending == 1) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();
+    // every thread is past the previous chunk: its ring slots may be refilled
+    issue_until(seq0 + kRStages);
+    const int beg = off[c], end = off[c + 1];
+    const int slot0 = int(seq0 % kRStages);
+    const int klast = int(p.k - (t0 + nt - 1) * kFBK);   // valid k in the chunk's last tile
+    // 64 groups of 4 lanes; lane `sub` owns k = sub, sub+4, ..., sub+28 of
+    // every tile of the chunk (column reads spread over banks).  Pass 1: group
+    // max of the products; pass 2: lowest k whose product equals it.  Trip
+    // counts are block-uniform, so every lane reaches the shuffles.
+    for (int e0 = beg; e0 < end; e0 += kFThreads / 4) {
+      const int e = e0 + grp;
+      const bool active = e < end;
+      const int o = active ? list[e] : 0;
       const int lr = o >> 7, lc = o & 127;
+      float best = Op::zero();
+      for (int j = 0; j < nt; ++j) {
+        const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
+        const float* st = smem + slot * kRStageFloats;
+        const int kc = j == nt - 1 ? klast : kFBK;
+        const float* arow = st + lr * kFApitch + sub;
+        const float* bcol = st + kFAStage + sub * kRBpitch + lc;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float pr = Op::mul(arow[4 * i], bcol[4 * i * kRBpitch]);
+          if (sub + 4 * i < kc && Op::better(pr, best)) best = pr;
+        }
+      }
+#pragma unroll
+      for (int d = 1; d < 4; d <<= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, best, d);
+        if (Op::better(other, best)) best = other;
+      }
       unsigned cand = 0xFFFFFFFFu;
       float cp = 0.f;
-      if (active) {
-        const float v = vcache[o];
-        const float4 av = *reinterpret_cast<const float4*>(As + lr * kFApitch + 4 * sub);
-        const float2 b01 = *reinterpret_cast<const float2*>(Bs + ((2 * sub) * kFBN + lc) * 2);
-        const float2 b23 = *reinterpret_cast<const float2*>(Bs + ((2 * sub + 1) * kFBN + lc) * 2);
-        const float pr[4] = {Op::mul(av.x, b01.x), Op::mul(av.y, b01.y), Op::mul(av.z, b23.x), Op::mul(av.w, b23.y)};
+      for (int j = nt - 1; j >= 0; --j) {
+        const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
+        const float* st = smem + slot * kRStageFloats;
+        const int kc = j == nt - 1 ? klast : kFBK;
+        const float* arow = st + lr * kFApitch + sub;
+        const float* bcol = st + kFAStage + sub * kRBpitch + lc;
 #pragma unroll
-        for (int i = 3; i >= 0; --i)
-          if (4 * sub + i < kcount && pr[i] == v) { cand = unsigned(4 * sub + i); cp = pr[i]; }
+        for (int i = 7; i >= 0; --i) {
+          const float pr = Op::mul(arow[4 * i], bcol[4 * i * kRBpitch]);
+          if (sub + 4 * i < kc && pr == best) { cand = unsigned(j * kFBK + sub + 4 * i); cp = pr; }
+        }
       }
-      unsigned best = cand;
+      unsigned first = cand;
 #pragma unroll
-      for (int d = 1; d < 8; d <<= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, d));
-      if (active && best != 0xFFFFFFFFu && cand == best) {
+      for (int d = 1; d < 4; d <<= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, d));
+      if (active && first != 0xFFFFFFFFu && cand == first) {
         const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
         C[gofs] = cp;
-        IDX[gofs] = int32_t(k0 + best);
-        atomicOr(&resolved[o >> 5], 1u << (o & 31));
+        IDX[gofs] = int32_t(t0 * kFBK + first);
       }
     }
-    advance(cur_chunk, cur_tile);
+    seq0 = need;
   }
   cp_async_wait<0>();
   TG_PHASE(4);
