@@ -483,50 +483,74 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
     // every tile of the chunk (column reads spread over banks).  Pass 1: group
     // max of the products; pass 2: lowest k whose product equals it.  Trip
     // counts are block-uniform, so every lane reaches the shuffles.
-    for (int e0 = beg; e0 < end; e0 += kFThreads / 4) {
-      const int e = e0 + grp;
-      const bool active = e < end;
-      const int o = active ? list[e] : 0;
-      const int lr = o >> 7, lc = o & 127;
-      float best = Op::zero();
-      for (int j = 0; j < nt; ++j) {
-        const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
-        const float* st = smem + slot * kRStageFloats;
-        const int kc = j == nt - 1 ? klast : kFBK;
-        const float* arow = st + lr * kFApitch + sub;
-        const float* bcol = st + kFAStage + sub * kRBpitch + lc;
+    // Each group handles two entries per round (independent chains for ILP);
+    // the products of pass 1 stay in registers for pass 2.
+    constexpr int kE = 2;
+    for (int e0 = beg; e0 < end; e0 += kE * (kFThreads / 4)) {
+      int o[kE];
+      bool active[kE];
+      float pr[kE][4][8];
+      float best[kE];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float pr = Op::mul(arow[4 * i], bcol[4 * i * kRBpitch]);
-          if (sub + 4 * i < kc && Op::better(pr, best)) best = pr;
+      for (int u = 0; u < kE; ++u) {
+        const int e = e0 + u * (kFThreads / 4) + grp;
+        active[u] = e < end;
+        o[u] = active[u] ? list[e] : 0;
+        best[u] = Op::zero();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j < nt) {
+          const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
+          const float* st = smem + slot * kRStageFloats;
+          const int kc = j == nt - 1 ? klast : kFBK;
+#pragma unroll
+          for (int u = 0; u < kE; ++u) {
+            const float* arow = st + (o[u] >> 7) * kFApitch + sub;
+            const float* bcol = st + kFAStage + sub * kRBpitch + (o[u] & 127);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              pr[u][j][i] = Op::mul(arow[4 * i], bcol[4 * i * kRBpitch]);
+              if (sub + 4 * i < kc && Op::better(pr[u][j][i], best[u])) best[u] = pr[u][j][i];
+            }
+          }
         }
       }
 #pragma unroll
-      for (int d = 1; d < 4; d <<= 1) {
-        const float other = __shfl_xor_sync(0xffffffffu, best, d);
-        if (Op::better(other, best)) best = other;
-      }
-      unsigned cand = 0xFFFFFFFFu;
-      float cp = 0.f;
-      for (int j = nt - 1; j >= 0; --j) {
-        const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
-        const float* st = smem + slot * kRStageFloats;
-        const int kc = j == nt - 1 ? klast : kFBK;
-        const float* arow = st + lr * kFApitch + sub;
-        const float* bcol = st + kFAStage + sub * kRBpitch + lc;
+      for (int u = 0; u < kE; ++u)
 #pragma unroll
-        for (int i = 7; i >= 0; --i) {
-          const float pr = Op::mul(arow[4 * i], bcol[4 * i * kRBpitch]);
-          if (sub + 4 * i < kc && pr == best) { cand = unsigned(j * kFBK + sub + 4 * i); cp = pr; }
+        for (int d = 1; d < 4; d <<= 1) {
+          const float other = __shfl_xor_sync(0xffffffffu, best[u], d);
+          if (Op::better(other, best[u])) best[u] = other;
+        }
+      unsigned cand[kE], first[kE];
+      float cp[kE];
+#pragma unroll
+      for (int u = 0; u < kE; ++u) { cand[u] = 0xFFFFFFFFu; cp[u] = 0.f; }
+#pragma unroll
+      for (int j = 3; j >= 0; --j) {
+        if (j < nt) {
+          const int kc = j == nt - 1 ? klast : kFBK;
+#pragma unroll
+          for (int u = 0; u < kE; ++u)
+#pragma unroll
+            for (int i = 7; i >= 0; --i)
+              if (sub + 4 * i < kc && pr[u][j][i] == best[u]) {
+                cand[u] = unsigned(j * kFBK + sub + 4 * i);
+                cp[u] = pr[u][j][i];
+              }
         }
       }
-      unsigned first = cand;
 #pragma unroll
-      for (int d = 1; d < 4; d <<= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, d));
-      if (active && first != 0xFFFFFFFFu && cand == first) {
-        const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
-        C[gofs] = cp;
-        IDX[gofs] = int32_t(t0 * kFBK + first);
+      for (int u = 0; u < kE; ++u) {
+        first[u] = cand[u];
+#pragma unroll
+        for (int d = 1; d < 4; d <<= 1) first[u] = min(first[u], __shfl_xor_sync(0xffffffffu, first[u], d));
+        if (active[u] && first[u] != 0xFFFFFFFFu && cand[u] == first[u]) {
+          const int64_t gofs = (m0 + (o[u] >> 7)) * p.ldc + (n0 + (o[u] & 127));
+          C[gofs] = cp[u];
+          IDX[gofs] = int32_t(t0 * kFBK + first[u]);
+        }
       }
     }
     seq0 = need;
