@@ -38,7 +38,7 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-M = N_ = K = 8192
+M = N_ = K = 8192  # --size overrides (small cases for ncu captures)
 SEED = 1
 METRIC = "Tropical ops/s (M*N*K/s) f32 MaxPlus+argmax 8192^3 per B200 (weak-scaled row shards for N>1)"
 UNIT = "tropical_ops/s"
@@ -208,37 +208,39 @@ def run_engine(args):
     ops_step = float(M) * N_ * K * world
     value = ops_step * args.steps / (total_ms * 1e-3)
 
-    # e2e through the public API with host buffers (pinned), rank-local
-    a_h = torch.from_numpy(a_np).pin_memory()
-    b_h = torch.from_numpy(b_np).pin_memory()
-    c_h = torch.empty((M * N_,), dtype=torch.float32).pin_memory()
-    am_h = torch.empty((M * N_,), dtype=torch.int32).pin_memory()
-    e2e_steps = max(1, min(args.steps, 5))
+    e2e_value = None
+    if not args.no_e2e:
+        # e2e through the public API with host buffers (pinned), rank-local
+        a_h = torch.from_numpy(a_np).pin_memory()
+        b_h = torch.from_numpy(b_np).pin_memory()
+        c_h = torch.empty((M * N_,), dtype=torch.float32).pin_memory()
+        am_h = torch.empty((M * N_,), dtype=torch.int32).pin_memory()
+        e2e_steps = max(1, min(args.steps, 5))
 
-    def e2e_step():
-        da = a_h.to(dev, non_blocking=True)
-        db = b_h.to(dev, non_blocking=True)
-        if dist is not None:
-            dist.broadcast(db, src=0)
-        cc, aa = tropical_gemm.maxplus_matmul_dlpack(da, db)
-        c_h.copy_(cc, non_blocking=True)
-        am_h.copy_(aa, non_blocking=True)
+        def e2e_step():
+            da = a_h.to(dev, non_blocking=True)
+            db = b_h.to(dev, non_blocking=True)
+            if dist is not None:
+                dist.broadcast(db, src=0)
+            cc, aa = tropical_gemm.maxplus_matmul_dlpack(da, db)
+            c_h.copy_(cc, non_blocking=True)
+            am_h.copy_(aa, non_blocking=True)
 
-    e2e_step()
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
         e2e_step()
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = ops_step * e2e_steps / (e2e_ms * 1e-3)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        if dist is not None:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_value = ops_step * e2e_steps / (e2e_ms * 1e-3)
 
     if rank == 0:
         peaks = measured_peaks()
@@ -351,9 +353,13 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    p.add_argument("--cpu-rows", type=int, default=64)
+    p.add_argument("--cpu-rows", type=int, default=1024)
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--size", type=int, default=8192, help="square size (8192 = BASELINE config 2a)")
     args = p.parse_args()
+    global M, N_, K
+    M = N_ = K = args.size
     if args.impl == "reference":
         run_reference(args)
     else:
