@@ -145,7 +145,8 @@ def dist_setup(n_gpus: int):
         world = int(os.environ.get("WORLD_SIZE", "1"))
         local = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        from tropical_gemm import distributed as D
+        D.init("nccl", timeout_s=300, device_id=torch.device("cuda", local))
         return dist, rank, world, local
     torch.cuda.set_device(0)
     return None, 0, 1, 0

@@ -1,0 +1,100 @@
+"""Multi-rank host logic of the row-sharded GEMM on CPU (gloo, world size 2).
+
+The GPU compute is replaced by the oracle here (passed as `compute`), so what
+is tested is the sharding, the broadcast of B and the gather; the GPU kernel
+is covered by the -m gpu tests.  Also: a rank that never joins makes the
+others fail with a timeout instead of hanging."""
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+
+import numpy as np
+import pytest
+
+from tropical_gemm.distributed import shard_rows
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("m,world", [(1, 2), (100, 2), (256, 2), (1000, 3), (8192 * 4, 4), (129, 8)])
+def test_shard_rows_partition(m, world):
+    spans = [shard_rows(m, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == m
+    for (a, b), (c, d) in zip(spans, spans[1:]):
+        assert b == c and a <= b
+    nonempty = [(a, b) for a, b in spans if b > a]
+    for a, b in nonempty:
+        assert a % 128 == 0
+    for a, b in nonempty[:-1]:
+        assert (b - a) % 128 == 0
+
+
+WORKER = textwrap.dedent('''
+    import os, sys
+    sys.path.insert(0, os.path.join(sys.argv[1], "tropical-gemm_b200")); sys.path.insert(0, sys.argv[1])
+    import numpy as np, torch
+    import torch.distributed as dist
+    from tropical_gemm import distributed as D
+    from oracle import tg_oracle as O
+    D.init("gloo", timeout_s=30)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    rng = np.random.default_rng(0)
+    m, k, n = 300, 70, 50
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b_full = rng.standard_normal((k, n)).astype(np.float32)
+    s, e = D.shard_rows(m, world, rank)
+    b = torch.from_numpy(b_full.copy()) if rank == 0 else torch.zeros((k, n))
+    def compute(semi, aa, bb, wa):
+        c, am = O.gemm(semi, aa.numpy(), bb.numpy(), wa)
+        return torch.from_numpy(c), torch.from_numpy(am)
+    c, am = D.sharded_matmul("maxplus", torch.from_numpy(a[s:e]), b, compute=compute)
+    assert torch.equal(b, torch.from_numpy(b_full))
+    C = D.gather_rows(c, m); AM = D.gather_rows(am, m)
+    c0, am0 = O.gemm("maxplus", a, b_full)
+    assert np.array_equal(C.numpy(), c0) and np.array_equal(AM.numpy(), am0)
+    dist.destroy_process_group()
+    print("rank", rank, "ok")
+''')
+
+
+def test_gloo_world2_sharded_matmul(tmp_path):
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER)
+    port = _free_port()
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                   CUDA_VISIBLE_DEVICES="")
+        procs.append(subprocess.Popen([sys.executable, str(script), ROOT], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = [p.communicate(timeout=180)[0] for p in procs]
+    for p, o in zip(procs, outs):
+        assert p.returncode == 0, o
+        assert "ok" in o
+
+
+def test_rank_that_never_joins_times_out(tmp_path):
+    script = tmp_path / "lonely.py"
+    script.write_text(textwrap.dedent('''
+        import os, sys, time
+        sys.path.insert(0, os.path.join(sys.argv[1], "tropical-gemm_b200"))
+        from tropical_gemm import distributed as D
+        t0 = time.time()
+        try:
+            D.init("gloo", timeout_s=3)
+            print("joined?!")
+        except Exception as e:
+            print("timeout after %.1f s: %s" % (time.time() - t0, type(e).__name__))
+    '''))
+    env = dict(os.environ, RANK="0", WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()),
+               CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, str(script), ROOT], env=env, capture_output=True, text=True, timeout=120)
+    assert "timeout after" in out.stdout, out.stdout + out.stderr

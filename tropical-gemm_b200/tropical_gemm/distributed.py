@@ -1,0 +1,76 @@
+"""Row-sharded tropical GEMM across the GPUs of one node.
+
+C = A (x) B where the rows of A (and of C / argmax) are split into contiguous
+blocks, one per rank, and B is needed whole by every rank.  The only exchange
+is one broadcast of B from its owner over NCCL (NVLink / NVSwitch on a B200
+node); C and argmax stay sharded, so no reduction is needed.  This is the
+multi-GPU layout the north-star names; the reference itself has no multi-GPU
+path (SURVEY: no collective call sites).
+
+One process per GPU, plumbing by torch.distributed.  Nothing here waits on a
+peer without a timeout: process groups are created with a finite timeout so a
+rank that never joins, or dies between steps, surfaces as an exception on the
+others instead of a hang.
+"""
+from datetime import timedelta
+from typing import Callable, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+
+ROW_ALIGN = 128  # rows per CTA tile of the fast kernel
+
+
+def shard_rows(m: int, world: int, rank: int, align: int = ROW_ALIGN) -> Tuple[int, int]:
+    """[start, stop) of the rows of an m-row A owned by `rank`.
+
+    Blocks are contiguous, ascending in rank, multiples of `align` except the
+    last non-empty one, and as even as the alignment allows.
+    """
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    units = (m + align - 1) // align
+    base, extra = divmod(units, world)
+    start_u = rank * base + min(rank, extra)
+    stop_u = start_u + base + (1 if rank < extra else 0)
+    return min(m, start_u * align), min(m, stop_u * align)
+
+
+def init(backend: str = "nccl", timeout_s: float = 60.0, **kw) -> None:
+    """init_process_group with a finite timeout (env:// rendezvous)."""
+    if not dist.is_initialized():
+        dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s), **kw)
+
+
+def broadcast_b(b: torch.Tensor, src: int = 0, group=None) -> torch.Tensor:
+    """Make every rank's `b` equal to the src rank's (in place)."""
+    dist.broadcast(b, src=src, group=group)
+    return b
+
+
+def sharded_matmul(semiring: str, a_local: torch.Tensor, b: torch.Tensor, src: int = 0, group=None,
+                   with_argmax: bool = True,
+                   compute: Optional[Callable] = None):
+    """Broadcast B from `src`, then C_local = A_local (x) B on this rank.
+
+    `a_local` is this rank's row block of A; `b` is a (K, N) buffer on every
+    rank (its contents matter only on `src`).  Returns (C_local, argmax_local).
+    `compute(semiring, a, b, with_argmax)` defaults to the engine's GEMM.
+    """
+    broadcast_b(b, src=src, group=group)
+    fn = compute or N.gemm
+    return fn(semiring, a_local, b, with_argmax)
+
+
+def gather_rows(x_local: torch.Tensor, m: int, group=None) -> torch.Tensor:
+    """All-gather row blocks (as produced by shard_rows) into the full matrix."""
+    world = dist.get_world_size(group)
+    rows = [shard_rows(m, world, r) for r in range(world)]
+    maxr = max(stop - start for start, stop in rows)
+    pad = torch.zeros((maxr,) + tuple(x_local.shape[1:]), dtype=x_local.dtype, device=x_local.device)
+    pad[: x_local.shape[0]] = x_local
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad, group=group)
+    return torch.cat([p[: stop - start] for p, (start, stop) in zip(parts, rows)], dim=0)
