@@ -226,3 +226,35 @@ def test_argmax_improvement_patterns(semi, pattern):
     c, am = engine(semi, a, b)
     c0, am0 = oracle(semi, a, b)
     assert same_bits(c, c0) and np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+def test_i32_out_of_range_falls_back_exactly(semi):
+    """Operands beyond the exact-in-f32 range (|x| > 2^23; MaxMul |x| > 4096)
+    take the exact integer kernel, including wrap-around on overflow."""
+    rng = np.random.default_rng(12)
+    a = rng.integers(-2**30, 2**30, (150, 90)).astype(np.int32)
+    b = rng.integers(-2**30, 2**30, (90, 140)).astype(np.int32)
+    for wa in (True, False):
+        c, am = engine(semi, a, b, wa)
+        c0, am0 = oracle(semi, a, b, wa)
+        assert same_bits(c, c0)
+        if wa:
+            assert np.array_equal(am, am0)
+
+
+def test_i32_apsp_step_with_sentinels():
+    """One APSP squaring step (BASELINE config 4 shape, reduced): 5% density,
+    weights 1..1000, missing = 46340, diagonal 0; ties are frequent."""
+    rng = np.random.default_rng(4)
+    n = 600
+    mask = rng.random((n, n)) < 0.05
+    w = rng.integers(1, 1001, (n, n)).astype(np.int32)
+    d = np.where(mask, w, 46340).astype(np.int32)
+    np.fill_diagonal(d, 0)
+    c, am = engine("minplus", d, d)
+    c0, am0 = oracle("minplus", d, d)
+    assert same_bits(c, c0) and np.array_equal(am, am0)
+    c2, am2 = engine("minplus", c, c)
+    c20, am20 = oracle("minplus", c0, c0)
+    assert same_bits(c2, c20) and np.array_equal(am2, am20)

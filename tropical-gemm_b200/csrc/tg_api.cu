@@ -73,9 +73,9 @@ bool fast_f32_ok(const Problem& P) {
   return true;
 }
 
-template <int S, bool ARGMAX>
-tg_status launch_fast_f32(const Problem& P, cudaStream_t st) {
-  auto kern = tg::fast_f32_kernel<S, ARGMAX>;
+template <int S, bool ARGMAX, bool OUTI = false>
+tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
+  auto kern = tg::fast_f32_kernel<S, ARGMAX, OUTI>;
   const size_t smem = ARGMAX ? tg::kFSmemArgmax : tg::kFSmemValues;
   static bool configured[64] = {false};
   int dev = 0;
@@ -100,7 +100,7 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st) {
     g.b = static_cast<const float*>(g.b) + b0 * g.sb;
     g.c = static_cast<float*>(g.c) + b0 * g.sc;
     if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
-    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec);
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec, acc_init);
     tg_status s = check_launch("fast_f32_kernel launch");
     if (s != TG_OK) return s;
   }
@@ -126,6 +126,84 @@ tg_status launch_generic(const Problem& P, cudaStream_t st) {
   return TG_OK;
 }
 
+// ---------------------------------------------------------------- i32 path
+// Integer MaxPlus / MinPlus / MaxMul are computed exactly in f32 when every
+// operand is small enough: |x| <= 2^23 for the additive semirings (sums stay
+// below 2^24, so every f32 sum is the exact integer sum and never wraps) and
+// |x| <= 4096 for MaxMul (products below 2^24).  The reference's sentinel
+// (+46340 for MinPlus, -46340 for MaxPlus; tropical_gemm.cu:15-50) becomes
+// +-inf, whose products never win, and the accumulator starts at the sentinel
+// itself, so a finite product equal to or beyond it never wins either --
+// exactly the saturating-add semantics.  Operands are converted into stream-
+// ordered scratch (cudaMallocAsync) together with an out-of-range flag; the
+// fast f32 kernel and the exact integer kernel are both enqueued behind that
+// flag, and whichever does not apply exits at once.  No host synchronisation.
+constexpr int64_t kI32FastMinOutputs = 128 * 128;
+
+template <int S>
+__global__ void i32_to_f32_kernel(const int32_t* __restrict__ src, float* __restrict__ dst, int64_t rows,
+                                  int64_t cols, int64_t ld, int64_t stride, int64_t dld, int* flag) {
+  const int32_t* s = src + int64_t(blockIdx.y) * stride;
+  float* d = dst + int64_t(blockIdx.y) * rows * dld;
+  const int64_t total = rows * cols;
+  const int32_t lim = S == tg::kMaxMul ? 4096 : (1 << 23);
+  bool bad = false;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int32_t x = s[(e / cols) * ld + e % cols];
+    float v;
+    if (S == tg::kMinPlus && x == tg::kInfI32) v = INFINITY;
+    else if (S == tg::kMaxPlus && x == -tg::kInfI32) v = -INFINITY;
+    else {
+      v = float(x);
+      if (x > lim || x < -lim) bad = true;
+    }
+    d[(e / cols) * dld + e % cols] = v;
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+}
+
+template <int S>
+tg_status launch_i32_via_f32(const Problem& P, cudaStream_t st) {
+  // scratch rows padded to 16 bytes (the fast kernel's vector loads)
+  const int64_t lda_f = (P.g.k + 3) & ~int64_t(3), ldb_f = (P.g.n + 3) & ~int64_t(3);
+  const int64_t asz = P.g.m * lda_f, bsz = P.g.k * ldb_f;
+  const size_t bytes = size_t(P.batch) * size_t(asz + bsz) * 4 + 256;
+  void* ws = nullptr;
+  cudaError_t e = cudaMallocAsync(&ws, bytes, st);
+  if (e != cudaSuccess) {  // no scratch: exact integer kernel only
+    cudaGetLastError();
+    return P.g.argmax ? launch_generic<S, int32_t, true>(P, st) : launch_generic<S, int32_t, false>(P, st);
+  }
+  int* flag = static_cast<int*>(ws);
+  float* af = reinterpret_cast<float*>(static_cast<char*>(ws) + 256);
+  float* bf = af + size_t(P.batch) * asz;
+  tg_status s = TG_OK;
+  if (cudaMemsetAsync(flag, 0, sizeof(int), st) != cudaSuccess) s = fail(TG_ERR_CUDA, "cudaMemsetAsync failed");
+  for (int64_t b0 = 0; s == TG_OK && b0 < P.batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
+    i32_to_f32_kernel<S><<<dim3(1024, unsigned(nb)), 256, 0, st>>>(
+        static_cast<const int32_t*>(P.g.a) + b0 * P.g.sa, af + b0 * asz, P.g.m, P.g.k, P.g.lda, P.g.sa, lda_f, flag);
+    i32_to_f32_kernel<S><<<dim3(1024, unsigned(nb)), 256, 0, st>>>(
+        static_cast<const int32_t*>(P.g.b) + b0 * P.g.sb, bf + b0 * bsz, P.g.k, P.g.n, P.g.ldb, P.g.sb, ldb_f, flag);
+    s = check_launch("i32_to_f32_kernel launch");
+  }
+  if (s == TG_OK) {
+    Problem F = P;
+    F.g.a = af; F.g.lda = lda_f; F.g.sa = asz;
+    F.g.b = bf; F.g.ldb = ldb_f; F.g.sb = bsz;
+    F.g.gate = flag; F.g.gate_run_if_set = 0;
+    const float init = S == tg::kMaxPlus ? -float(tg::kInfI32) : (S == tg::kMinPlus ? float(tg::kInfI32) : 0.0f);
+    s = P.g.argmax ? launch_fast_f32<S, true, true>(F, st, init) : launch_fast_f32<S, false, true>(F, st, init);
+  }
+  if (s == TG_OK) {
+    Problem X = P;
+    X.g.gate = flag; X.g.gate_run_if_set = 1;
+    s = P.g.argmax ? launch_generic<S, int32_t, true>(X, st) : launch_generic<S, int32_t, false>(X, st);
+  }
+  cudaFreeAsync(ws, st);
+  return s;
+}
+
 template <int S, typename T>
 tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
   const bool am = P.g.argmax != nullptr;
@@ -141,7 +219,11 @@ tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
     return TG_OK;
   }
   if constexpr (std::is_same<T, float>::value) {
-    if (fast_f32_ok(P)) return am ? launch_fast_f32<S, true>(P, st) : launch_fast_f32<S, false>(P, st);
+    const float z = S == tg::kMaxPlus ? -INFINITY : (S == tg::kMinPlus ? INFINITY : 0.0f);
+    if (fast_f32_ok(P)) return am ? launch_fast_f32<S, true>(P, st, z) : launch_fast_f32<S, false>(P, st, z);
+  }
+  if constexpr (std::is_same<T, int32_t>::value) {
+    if (P.g.m * P.g.n >= kI32FastMinOutputs) return launch_i32_via_f32<S>(P, st);
   }
   return am ? launch_generic<S, T, true>(P, st) : launch_generic<S, T, false>(P, st);
 }

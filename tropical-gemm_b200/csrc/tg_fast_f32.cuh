@@ -27,6 +27,7 @@
 #pragma once
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
+#include <type_traits>
 
 namespace tg {
 
@@ -268,10 +269,21 @@ __device__ __forceinline__ void fix_k_tail(float* stage, int kvalid, int tid) {
   }
 }
 
-template <int S, bool ARGMAX>
+// OUTI: C is int32 (the i32 path computes exactly in f32 on converted
+// operands and converts the result back).  acc_init: accumulator start value
+// (the semiring zero for f32; the reference's integer sentinel for i32 --
+// the sentinel operands themselves are mapped to +-inf by the conversion).
+template <typename CT>
+__device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
+  if constexpr (sizeof(CT) == 4 && !std::is_same<CT, float>::value) C[o] = CT(v); else C[o] = v;
+}
+
+template <int S, bool ARGMAX, bool OUTI = false>
 __global__ void __launch_bounds__(kFThreads, 1)
-fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
+fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   using Op = FastOps<S>;
+  using CT = typename std::conditional<OUTI, int32_t, float>::type;
+  if (gated_off(p)) return;
   extern __shared__ __align__(16) float smem[];
   unsigned char* sbytes = reinterpret_cast<unsigned char*>(smem);
   const int tid = threadIdx.x;
@@ -282,7 +294,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
   const int64_t batch = blockIdx.z;
   const float* __restrict__ A = static_cast<const float*>(p.a) + batch * p.sa;
   const float* __restrict__ B = static_cast<const float*>(p.b) + batch * p.sb;
-  float* __restrict__ C = static_cast<float*>(p.c) + batch * p.sc;
+  CT* __restrict__ C = static_cast<CT*>(p.c) + batch * p.sc;
   int32_t* __restrict__ IDX = ARGMAX ? p.argmax + batch * p.sc : nullptr;
   const int64_t m0 = int64_t(blockIdx.x) * kFBM;
   const int64_t n0 = int64_t(blockIdx.y) * kFBN;
@@ -301,8 +313,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
   for (int r = 0; r < 8; ++r)
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      acc[r][c] = Op::zero();
-      if (ARGMAX) snap[r][c] = Op::zero();
+      acc[r][c] = acc_init;
+      if (ARGMAX) snap[r][c] = acc_init;
     }
 
   // ------------------------------------------------------------ main loop
@@ -383,9 +395,9 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
         continue;
       }
       if (!ARGMAX) {
-        C[gr * p.ldc + gc] = acc[r][c];
+        store_c(C, gr * p.ldc + gc, acc[r][c]);
       } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
-        C[gr * p.ldc + gc] = Op::zero();
+        store_c(C, gr * p.ldc + gc, acc_init);
         IDX[gr * p.ldc + gc] = 0;
       }
     }
@@ -548,7 +560,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec) {
         for (int d = 1; d < 4; d <<= 1) first[u] = min(first[u], __shfl_xor_sync(0xffffffffu, first[u], d));
         if (active[u] && first[u] != 0xFFFFFFFFu && cand[u] == first[u]) {
           const int64_t gofs = (m0 + (o[u] >> 7)) * p.ldc + (n0 + (o[u] & 127));
-          C[gofs] = cp[u];
+          store_c(C, gofs, cp[u]);
           IDX[gofs] = int32_t(t0 * kFBK + first[u]);
         }
       }

@@ -21,7 +21,17 @@ struct GemmArgs {
   const void* b; int64_t ldb, sb;
   void* c;       int64_t ldc, sc;
   int32_t* argmax;
+  // Optional device-side gate: when set, the kernel runs only if
+  // (*gate != 0) == (gate_run_if_set != 0).  Lets the host enqueue both a
+  // fast and an exact kernel behind a device-computed precondition without
+  // a host synchronisation.
+  const int* gate = nullptr;
+  int gate_run_if_set = 0;
 };
+
+__device__ __forceinline__ bool gated_off(const GemmArgs& p) {
+  return p.gate && ((*p.gate != 0) != (p.gate_run_if_set != 0));
+}
 
 constexpr int kGenBM = 64, kGenBN = 64, kGenBK = 16, kGenThreads = 256;
 
@@ -29,6 +39,7 @@ template <int S, typename T, bool ARGMAX>
 __global__ void __launch_bounds__(kGenThreads)
 generic_gemm_kernel(GemmArgs p) {
   using R = Ring<S, T>;
+  if (gated_off(p)) return;
   __shared__ T As[kGenBK][kGenBM];
   __shared__ T Bs[kGenBK][kGenBN];
 
