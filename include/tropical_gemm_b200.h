@@ -118,6 +118,30 @@ tg_status tg_backward_b(tg_semiring semiring, tg_dtype dtype, tg_layout layout,
                         void* grad_b, int64_t ldb, int64_t stride_b,
                         int accumulate, void* stream);
 
+/* Integer (i32) C = A (x) B, optionally with argmax, that allocates nothing.
+ * No counterpart in the reference: it is an addition of this library.
+ * For callers that cannot allocate device memory at call time -- e.g. a host
+ * framework that has reserved the GPU's memory for its own pool, or a
+ * serving / real-time loop that forbids cudaMalloc after start-up because an
+ * allocation can block, fail or synchronise.  Same arguments and results as
+ * tg_gemm with dtype TG_I32 (one matrix, no batch).  Its scratch (A and B as
+ * f32, rows padded to 4 elements, plus a 256-byte header) lives in a fixed
+ * 64 MiB device array that every GPU loading this library keeps until the
+ * process exits; larger problems are rejected with TG_ERR_UNSUPPORTED and a
+ * message (use tg_gemm for them).  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the one array and it keeps the last
+ * call's contents: calls that overlap on the GPU (different streams, or
+ * different host threads on the same device) race and must be serialised by
+ * the caller. */
+tg_status tg_gemm_i32_noalloc(tg_semiring semiring, tg_layout layout,
+                              int64_t m, int64_t n, int64_t k,
+                              const void* a, int64_t lda,
+                              const void* b, int64_t ldb,
+                              void* c, int64_t ldc,
+                              int32_t* argmax,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

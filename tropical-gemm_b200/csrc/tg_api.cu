@@ -16,6 +16,7 @@
 #include <cstring>
 #include <string>
 #include <algorithm>
+#include <mutex>
 #include <cuda_runtime.h>
 #include "../../include/tropical_gemm_b200.h"
 #include "tg_semiring.cuh"
@@ -423,3 +424,114 @@ extern "C" int tg_debug_phase_ts(long long* host, int n) {
   return (int)cudaMemcpyFromSymbol(host, tg::tg_phase_ts, sizeof(long long) * n);
 }
 #endif
+
+// --------------------------------------------------------------------------
+// Allocation-free variant of the i32 GEMM.
+//
+// Some callers cannot allocate device memory at call time: a host framework
+// that has already reserved the GPU's memory for its own pool, or a serving
+// or real-time loop that forbids cudaMalloc/cudaMallocAsync after start-up
+// (an allocation can block, fail under memory pressure, or synchronise).
+// tg_gemm_i32_noalloc gives them the i32 GEMM without any allocation: its
+// scratch (the f32 copies of A and B plus the range flag) lives in the
+// fixed array below, which every GPU that loads this library keeps for the
+// life of the process.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;   // 64 MiB per device
+static __device__ __align__(256) unsigned char tg_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of tg_noalloc_scratch, looked up once per device (the
+// symbol's host-side name is not a device address).
+void* noalloc_scratch_address(int dev, tg_status* st) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  if (dev < 0 || dev >= 64) { *st = fail(TG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev); return nullptr; }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, tg_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *st = fail(TG_ERR_CUDA, "cudaGetSymbolAddress(tg_noalloc_scratch): %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *st = TG_OK;
+  return addr[dev];
+}
+
+template <int S>
+tg_status noalloc_i32(const Problem& P, cudaStream_t st, unsigned char* ws) {
+  const int64_t lda_f = (P.g.k + 3) & ~int64_t(3), ldb_f = (P.g.n + 3) & ~int64_t(3);
+  const int64_t asz = P.g.m * lda_f, bsz = P.g.k * ldb_f;
+  int* flag = reinterpret_cast<int*>(ws);
+  float* af = reinterpret_cast<float*>(ws + 256);
+  float* bf = af + asz;
+  // the array keeps the previous call's contents: the flag must start at zero
+  if (cudaMemsetAsync(flag, 0, sizeof(int), st) != cudaSuccess) return fail(TG_ERR_CUDA, "cudaMemsetAsync failed");
+  i32_to_f32_kernel<S><<<dim3(1024, 1), 256, 0, st>>>(static_cast<const int32_t*>(P.g.a), af, P.g.m, P.g.k,
+                                                      P.g.lda, 0, lda_f, flag);
+  i32_to_f32_kernel<S><<<dim3(1024, 1), 256, 0, st>>>(static_cast<const int32_t*>(P.g.b), bf, P.g.k, P.g.n,
+                                                      P.g.ldb, 0, ldb_f, flag);
+  tg_status s = check_launch("i32_to_f32_kernel launch");
+  if (s != TG_OK) return s;
+  Problem F = P;
+  F.g.a = af; F.g.lda = lda_f; F.g.sa = asz;
+  F.g.b = bf; F.g.ldb = ldb_f; F.g.sb = bsz;
+  F.g.gate = flag; F.g.gate_run_if_set = 0;
+  const float init = S == tg::kMaxPlus ? -float(tg::kInfI32) : (S == tg::kMinPlus ? float(tg::kInfI32) : 0.0f);
+  s = P.g.argmax ? launch_fast_f32<S, true, true>(F, st, init) : launch_fast_f32<S, false, true>(F, st, init);
+  if (s != TG_OK) return s;
+  Problem X = P;
+  X.g.gate = flag; X.g.gate_run_if_set = 1;
+  return P.g.argmax ? launch_generic<S, int32_t, true>(X, st) : launch_generic<S, int32_t, false>(X, st);
+}
+
+}  // namespace
+
+extern "C" tg_status tg_gemm_i32_noalloc(tg_semiring semiring, tg_layout layout, int64_t m, int64_t n, int64_t k,
+                                         const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
+                                         int64_t ldc, int32_t* argmax, void* stream) {
+  g_last_error.clear();
+  if (semiring < TG_MAXPLUS || semiring > TG_MAXMUL) return fail(TG_ERR_INVALID_ARGUMENT, "unknown semiring %d", int(semiring));
+  if (layout != TG_ROW_MAJOR && layout != TG_COL_MAJOR) return fail(TG_ERR_INVALID_ARGUMENT, "unknown layout %d", int(layout));
+  if (m < 0 || n < 0 || k < 0) return fail(TG_ERR_INVALID_ARGUMENT, "negative size (m=%lld n=%lld k=%lld)", (long long)m, (long long)n, (long long)k);
+  if (m == 0 || n == 0) return TG_OK;
+  if (!c) return fail(TG_ERR_INVALID_ARGUMENT, "C is null");
+  if (k > 0 && (!a || !b)) return fail(TG_ERR_INVALID_ARGUMENT, "A or B is null");
+  const bool row = layout == TG_ROW_MAJOR;
+  const int64_t need_lda = row ? k : m, need_ldb = row ? n : k, need_ldc = row ? n : m;
+  if (k > 0 && lda < std::max<int64_t>(1, need_lda)) return fail(TG_ERR_DIMENSION_MISMATCH, "lda=%lld < %lld", (long long)lda, (long long)need_lda);
+  if (k > 0 && ldb < std::max<int64_t>(1, need_ldb)) return fail(TG_ERR_DIMENSION_MISMATCH, "ldb=%lld < %lld", (long long)ldb, (long long)need_ldb);
+  if (ldc < std::max<int64_t>(1, need_ldc)) return fail(TG_ERR_DIMENSION_MISMATCH, "ldc=%lld < %lld", (long long)ldc, (long long)need_ldc);
+  Problem P;
+  P.batch = 1;
+  P.g = row ? tg::GemmArgs{m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, argmax}
+            : tg::GemmArgs{n, m, k, b, ldb, 0, a, lda, 0, c, ldc, 0, argmax};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k == 0) {   // no scratch needed: semiring zero and index 0
+    switch (semiring) {
+      case TG_MAXPLUS: return dispatch_typed<tg::kMaxPlus, int32_t>(P, st);
+      case TG_MINPLUS: return dispatch_typed<tg::kMinPlus, int32_t>(P, st);
+      default: return dispatch_typed<tg::kMaxMul, int32_t>(P, st);
+    }
+  }
+  const int64_t lda_f = (P.g.k + 3) & ~int64_t(3), ldb_f = (P.g.n + 3) & ~int64_t(3);
+  const double need = 256.0 + 4.0 * (double(P.g.m) * double(lda_f) + double(P.g.k) * double(ldb_f));
+  if (need > double(kNoAllocScratchBytes))
+    return fail(TG_ERR_UNSUPPORTED,
+                "tg_gemm_i32_noalloc: A and B need %.0f bytes of scratch as f32 (rows padded to 4 elements), "
+                "more than the fixed %zu-byte scratch; use tg_gemm instead",
+                need, kNoAllocScratchBytes);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(TG_ERR_NO_DEVICE, "no current CUDA device");
+  tg_status s;
+  unsigned char* ws = static_cast<unsigned char*>(noalloc_scratch_address(dev, &s));
+  if (!ws) return s;
+  switch (semiring) {
+    case TG_MAXPLUS: return noalloc_i32<tg::kMaxPlus>(P, st, ws);
+    case TG_MINPLUS: return noalloc_i32<tg::kMinPlus>(P, st, ws);
+    default: return noalloc_i32<tg::kMaxMul>(P, st, ws);
+  }
+}
