@@ -138,6 +138,63 @@ def cpu_baseline(rows: int, threads: int):
     return rows * N_ * K / dt, dt
 
 
+def _time_ms(fn, reps=3, warm=1):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def extras(dev):
+    """The other BASELINE configs on one GPU (informational keys, same metric)."""
+    from tropical_gemm import _native as Nat
+    from tropical_gemm.pytorch import tropical_maxplus_matmul_batched
+    res = {}
+    rng = np.random.default_rng(1)
+    # 2a without argmax
+    a = torch.from_numpy(rng.standard_normal((8192, 8192), dtype=np.float32)).to(dev)
+    b = torch.from_numpy(rng.standard_normal((8192, 8192), dtype=np.float32)).to(dev)
+    ms = _time_ms(lambda: Nat.gemm("maxplus", a, b, False))
+    res["maxplus_f32_value_only_8192"] = {"ops_per_s": 8192.0 ** 3 / (ms * 1e-3), "ms": ms}
+    # 2b: MinPlus f32 + argmax, values U[0,100) with 90% +inf
+    mats = []
+    for _ in range(2):
+        v = (100 * rng.random((8192, 8192))).astype(np.float32)
+        v[rng.random((8192, 8192)) < 0.9] = np.inf
+        mats.append(torch.from_numpy(v).to(dev))
+    ms = _time_ms(lambda: Nat.gemm("minplus", mats[0], mats[1], True))
+    res["minplus_f32_argmax_90pct_inf_8192"] = {"ops_per_s": 8192.0 ** 3 / (ms * 1e-3), "ms": ms}
+    del a, b, mats
+    # 3: batched autograd forward + backward, 64 x [512x256] . [256x512]
+    g = torch.Generator().manual_seed(0)
+    ab = torch.randn((64, 512, 256), generator=g).to(dev).requires_grad_(True)
+    bb = torch.randn((64, 256, 512), generator=g).to(dev).requires_grad_(True)
+
+    def step():
+        ab.grad = None
+        bb.grad = None
+        tropical_maxplus_matmul_batched(ab, bb).sum().backward()
+
+    ms = _time_ms(step, reps=10, warm=3)
+    res["batched_autograd_fwd_bwd_64x512x256x512"] = {"ms": ms, "fwd_ops_per_s": 64 * 512 * 256 * 512 / (ms * 1e-3)}
+    # 4: one APSP squaring, MinPlus i32, n = 16384, 5% density, weights 1..1000, missing = 46340
+    n = 16384
+    mask = rng.random((n, n)) < 0.05
+    d = np.where(mask, rng.integers(1, 1001, (n, n)), 46340).astype(np.int32)
+    np.fill_diagonal(d, 0)
+    td = torch.from_numpy(d).to(dev)
+    ms = _time_ms(lambda: Nat.gemm("minplus", td, td, True), reps=2)
+    res["apsp_minplus_i32_argmax_16384_one_squaring"] = {"ops_per_s": float(n) ** 3 / (ms * 1e-3), "ms": ms,
+                                                         "14_squarings_s": 14 * ms / 1e3}
+    return res
+
+
 def dist_setup(n_gpus: int):
     if n_gpus > 1 or "RANK" in os.environ:
         import torch.distributed as dist
@@ -280,6 +337,8 @@ def run_engine(args):
             "clocks": clocks,
             "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
         }
+        if world == 1 and not args.no_extras and args.size == 8192:
+            out["extras"] = extras(dev)
         if world == 1 and not args.no_cpu:
             rows = args.cpu_rows
             threads = os.cpu_count() or 1
@@ -357,6 +416,7 @@ def main():
     p.add_argument("--cpu-rows", type=int, default=1024)
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-extras", action="store_true", help="skip the other BASELINE configs (extra keys)")
     p.add_argument("--size", type=int, default=8192, help="square size (8192 = BASELINE config 2a)")
     args = p.parse_args()
     global M, N_, K
