@@ -497,6 +497,56 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
     // counts are block-uniform, so every lane reaches the shuffles.
     // Each group handles two entries per round (independent chains for ILP);
     // the products of pass 1 stay in registers for pass 2.
+    if (nt == 2 && klast == kFBK) {
+      // Full two-tile chunk (every chunk but possibly the last): no k-range
+      // masks; pass 1 is a max3 tree, pass 2 a 16-bit equality mask whose
+      // lowest set bit is the lane's first winning k (bit order = k order).
+      const float* st0 = smem + slot0 * kRStageFloats;
+      const float* st1 = smem + (slot0 + 1 >= kRStages ? slot0 + 1 - kRStages : slot0 + 1) * kRStageFloats;
+      for (int e0 = beg; e0 < end; e0 += 2 * (kFThreads / 4)) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int e = e0 + u * (kFThreads / 4) + grp;
+          const bool act = e < end;
+          const int o = act ? list[e] : 0;
+          const int lr = o >> 7, lc = o & 127;
+          float pv[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pv[i] = Op::mul(st0[lr * kFApitch + sub + 4 * i], st0[kFAStage + (sub + 4 * i) * kRBpitch + lc]);
+            pv[8 + i] = Op::mul(st1[lr * kFApitch + sub + 4 * i], st1[kFAStage + (sub + 4 * i) * kRBpitch + lc]);
+          }
+          float m = Op::red3(Op::red3(Op::red3(pv[0], pv[1], pv[2]), Op::red3(pv[3], pv[4], pv[5]),
+                                      Op::red3(pv[6], pv[7], pv[8])),
+                             Op::red3(Op::red3(pv[9], pv[10], pv[11]), Op::red3(pv[12], pv[13], pv[14]), pv[15]),
+                             pv[15]);
+          float x = __shfl_xor_sync(0xffffffffu, m, 1);
+          m = Op::red3(m, x, x);
+          x = __shfl_xor_sync(0xffffffffu, m, 2);
+          m = Op::red3(m, x, x);
+          unsigned mask = 0;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) mask |= (pv[q] == m) ? (1u << q) : 0u;
+          unsigned kf = 0xFFFFFFFFu;
+          if (mask) {
+            const int q = __ffs(mask) - 1;
+            kf = unsigned(32 * (q >> 3) + sub + 4 * (q & 7));
+          }
+          unsigned first = min(kf, __shfl_xor_sync(0xffffffffu, kf, 1));
+          first = min(first, __shfl_xor_sync(0xffffffffu, first, 2));
+          if (act && first != 0xFFFFFFFFu && kf == first) {
+            const float* st = first >= unsigned(kFBK) ? st1 : st0;
+            const int kk = int(first) & (kFBK - 1);
+            const float v = Op::mul(st[lr * kFApitch + kk], st[kFAStage + kk * kRBpitch + lc]);
+            const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
+            store_c(C, gofs, v);
+            IDX[gofs] = int32_t(t0 * kFBK + first);
+          }
+        }
+      }
+      seq0 = need;
+      continue;
+    }
     constexpr int kE = 2;
     for (int e0 = beg; e0 < end; e0 += kE * (kFThreads / 4)) {
       int o[kE];
