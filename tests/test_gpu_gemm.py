@@ -258,3 +258,17 @@ def test_i32_apsp_step_with_sentinels():
     c2, am2 = engine("minplus", c, c)
     c20, am20 = oracle("minplus", c0, c0)
     assert same_bits(c2, c20) and np.array_equal(am2, am20)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+def test_i64_out_of_range_falls_back_exactly(semi):
+    """i64 operands beyond the exact-in-f64 range take the exact integer kernel."""
+    rng = np.random.default_rng(13)
+    a = rng.integers(-2**62, 2**62, (140, 70)).astype(np.int64)
+    b = rng.integers(-2**62, 2**62, (70, 150)).astype(np.int64)
+    for wa in (True, False):
+        c, am = engine(semi, a, b, wa)
+        c0, am0 = oracle(semi, a, b, wa)
+        assert same_bits(c, c0)
+        if wa:
+            assert np.array_equal(am, am0)

@@ -23,6 +23,7 @@
 #include "tg_generic.cuh"
 #include "tg_fast_f32.cuh"
 #include "tg_backward.cuh"
+#include "tg_wide.cuh"
 
 namespace {
 
@@ -103,6 +104,34 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
     if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
     kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec, acc_init);
     tg_status s = check_launch("fast_f32_kernel launch");
+    if (s != TG_OK) return s;
+  }
+  return TG_OK;
+}
+
+template <int S, bool ARGMAX, bool OUTI = false>
+tg_status launch_wide_f64(const Problem& P, cudaStream_t st, double acc_init) {
+  auto kern = tg::wide_f64_kernel<S, ARGMAX, OUTI>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tg::kWSmem));
+    if (e != cudaSuccess) return fail(TG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  const int64_t gx = (P.g.m + tg::kWBM - 1) / tg::kWBM;
+  const int64_t gy = (P.g.n + tg::kWBN - 1) / tg::kWBN;
+  if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
+  for (int64_t b0 = 0; b0 < P.batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
+    tg::GemmArgs g = P.g;
+    g.a = static_cast<const double*>(g.a) + b0 * g.sa;
+    g.b = static_cast<const double*>(g.b) + b0 * g.sb;
+    g.c = static_cast<double*>(g.c) + b0 * g.sc;
+    if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kWThreads, tg::kWSmem, st>>>(g, acc_init);
+    tg_status s = check_launch("wide_f64_kernel launch");
     if (s != TG_OK) return s;
   }
   return TG_OK;
@@ -205,6 +234,72 @@ tg_status launch_i32_via_f32(const Problem& P, cudaStream_t st) {
   return s;
 }
 
+// ---------------------------------------------------------------- i64 path
+// Same idea as the i32 path, in f64: exact while |x| <= 2^51 (additive; sums
+// below 2^52) or |x| <= 2^26 (MaxMul; products below 2^52); the sentinel
+// +-3037000499 becomes +-inf and the accumulator starts at the sentinel.
+template <int S>
+__global__ void i64_to_f64_kernel(const int64_t* __restrict__ src, double* __restrict__ dst, int64_t rows,
+                                  int64_t cols, int64_t ld, int64_t stride, int64_t dld, int* flag) {
+  const int64_t* s = src + int64_t(blockIdx.y) * stride;
+  double* d = dst + int64_t(blockIdx.y) * rows * dld;
+  const int64_t total = rows * cols;
+  const int64_t lim = S == tg::kMaxMul ? (int64_t(1) << 26) : (int64_t(1) << 51);
+  bool bad = false;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t x = s[(e / cols) * ld + e % cols];
+    double v;
+    if (S == tg::kMinPlus && x == tg::kInfI64) v = INFINITY;
+    else if (S == tg::kMaxPlus && x == -tg::kInfI64) v = -INFINITY;
+    else {
+      v = double(x);
+      if (x > lim || x < -lim) bad = true;
+    }
+    d[(e / cols) * dld + e % cols] = v;
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+}
+
+template <int S>
+tg_status launch_i64_via_f64(const Problem& P, cudaStream_t st) {
+  const int64_t lda_f = (P.g.k + 1) & ~int64_t(1), ldb_f = (P.g.n + 1) & ~int64_t(1);
+  const int64_t asz = P.g.m * lda_f, bsz = P.g.k * ldb_f;
+  const size_t bytes = size_t(P.batch) * size_t(asz + bsz) * 8 + 256;
+  void* ws = nullptr;
+  if (cudaMallocAsync(&ws, bytes, st) != cudaSuccess) {
+    cudaGetLastError();
+    return P.g.argmax ? launch_generic<S, int64_t, true>(P, st) : launch_generic<S, int64_t, false>(P, st);
+  }
+  int* flag = static_cast<int*>(ws);
+  double* af = reinterpret_cast<double*>(static_cast<char*>(ws) + 256);
+  double* bf = af + size_t(P.batch) * asz;
+  tg_status s = TG_OK;
+  if (cudaMemsetAsync(flag, 0, sizeof(int), st) != cudaSuccess) s = fail(TG_ERR_CUDA, "cudaMemsetAsync failed");
+  for (int64_t b0 = 0; s == TG_OK && b0 < P.batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
+    i64_to_f64_kernel<S><<<dim3(1024, unsigned(nb)), 256, 0, st>>>(
+        static_cast<const int64_t*>(P.g.a) + b0 * P.g.sa, af + b0 * asz, P.g.m, P.g.k, P.g.lda, P.g.sa, lda_f, flag);
+    i64_to_f64_kernel<S><<<dim3(1024, unsigned(nb)), 256, 0, st>>>(
+        static_cast<const int64_t*>(P.g.b) + b0 * P.g.sb, bf + b0 * bsz, P.g.k, P.g.n, P.g.ldb, P.g.sb, ldb_f, flag);
+    s = check_launch("i64_to_f64_kernel launch");
+  }
+  if (s == TG_OK) {
+    Problem F = P;
+    F.g.a = af; F.g.lda = lda_f; F.g.sa = asz;
+    F.g.b = bf; F.g.ldb = ldb_f; F.g.sb = bsz;
+    F.g.gate = flag; F.g.gate_run_if_set = 0;
+    const double init = S == tg::kMaxPlus ? -double(tg::kInfI64) : (S == tg::kMinPlus ? double(tg::kInfI64) : 0.0);
+    s = P.g.argmax ? launch_wide_f64<S, true, true>(F, st, init) : launch_wide_f64<S, false, true>(F, st, init);
+  }
+  if (s == TG_OK) {
+    Problem X = P;
+    X.g.gate = flag; X.g.gate_run_if_set = 1;
+    s = P.g.argmax ? launch_generic<S, int64_t, true>(X, st) : launch_generic<S, int64_t, false>(X, st);
+  }
+  cudaFreeAsync(ws, st);
+  return s;
+}
+
 template <int S, typename T>
 tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
   const bool am = P.g.argmax != nullptr;
@@ -225,6 +320,16 @@ tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
   }
   if constexpr (std::is_same<T, int32_t>::value) {
     if (P.g.m * P.g.n >= kI32FastMinOutputs) return launch_i32_via_f32<S>(P, st);
+  }
+  if constexpr (std::is_same<T, double>::value) {
+    const double z = S == tg::kMaxPlus ? -double(INFINITY) : (S == tg::kMinPlus ? double(INFINITY) : 0.0);
+    // argmax: the wide kernel (strict update, ~1.03x the reference kernel's
+    // rate at 4096^3 and faster at large tiles); value-only: the generic kernel,
+    // whose fmax fold measured faster than the wide kernel's sign-exact select
+    if (am) return launch_wide_f64<S, true>(P, st, z);
+  }
+  if constexpr (std::is_same<T, int64_t>::value) {
+    if (P.g.m * P.g.n >= kI32FastMinOutputs) return launch_i64_via_f64<S>(P, st);
   }
   return am ? launch_generic<S, T, true>(P, st) : launch_generic<S, T, false>(P, st);
 }
