@@ -75,11 +75,24 @@ bool fast_f32_ok(const Problem& P) {
   return true;
 }
 
+constexpr int64_t kPairMaxK = 512;
+
 template <int S, bool ARGMAX, bool OUTI = false>
 tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
   auto kern = tg::fast_f32_kernel<S, ARGMAX, OUTI>;
   const size_t smem = ARGMAX ? tg::kFSmemArgmax : tg::kFSmemValues;
   static bool configured[64] = {false};
+  if (ARGMAX && P.g.k <= kPairMaxK) {   // configure the pair-tracking variant too
+    static bool configured_pair[64] = {false};
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d < 64 && !configured_pair[d]) {
+      cudaError_t e = cudaFuncSetAttribute(tg::fast_f32_kernel<S, ARGMAX, OUTI, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      if (e != cudaSuccess) return fail(TG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      configured_pair[d] = true;
+    }
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
@@ -92,6 +105,9 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
   const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
                      (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
   while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
+  // Short K: the re-stream costs as much per output as at long K, so track
+  // the argmax per k-pair in registers instead (measured crossover ~K = 512).
+  if (ARGMAX && P.g.k <= kPairMaxK) kern = tg::fast_f32_kernel<S, ARGMAX, OUTI, true>;
   const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;
   const int64_t gy = (P.g.n + tg::kFBN - 1) / tg::kFBN;
   if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");

@@ -278,7 +278,13 @@ __device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
   if constexpr (sizeof(CT) == 4 && !std::is_same<CT, float>::value) C[o] = CT(v); else C[o] = v;
 }
 
-template <int S, bool ARGMAX, bool OUTI = false>
+// PAIR (with ARGMAX, for short K): instead of chunk detection + re-stream,
+// track the winner per k-pair in registers -- after each FADD2/FMNMX3 step a
+// strict compare of the new running value against the old one, and on an
+// improvement the first of the two products that attains it (value bits and
+// index).  ~3 instructions per product instead of ~1, but no re-stream,
+// whose cost per output does not shrink with K.
+template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false>
 __global__ void __launch_bounds__(kFThreads, 1)
 fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   using Op = FastOps<S>;
@@ -303,18 +309,20 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
 
   const TileLoader ldr(A, B, p, m0, n0, tid, smem);
   uint16_t* cid = reinterpret_cast<uint16_t*>(sbytes + kOffCid);
-  if (ARGMAX) {
+  if (ARGMAX && !PAIR) {
     for (int i = tid; i < kFBM * kFBN; i += kFThreads) cid[i] = kNoChunk;
   }
 
   float acc[8][8];
-  float snap[ARGMAX ? 8 : 1][ARGMAX ? 8 : 1];
+  float snap[ARGMAX && !PAIR ? 8 : 1][ARGMAX && !PAIR ? 8 : 1];
+  int32_t pidx[PAIR ? 8 : 1][PAIR ? 8 : 1];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       acc[r][c] = acc_init;
-      if (ARGMAX) snap[r][c] = acc_init;
+      if (ARGMAX && !PAIR) snap[r][c] = acc_init;
+      if (PAIR) pidx[r][c] = 0;
     }
 
   // ------------------------------------------------------------ main loop
@@ -357,15 +365,30 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             float lo, hi;
-            Op::pair(lo, hi, a0, a1, bq[q].x, bq[q].y);
-            acc[r][2 * q] = Op::red3(acc[r][2 * q], lo, hi);
-            Op::pair(lo, hi, a0, a1, bq[q].z, bq[q].w);
-            acc[r][2 * q + 1] = Op::red3(acc[r][2 * q + 1], lo, hi);
+            if (PAIR) {
+              const int32_t kg = int32_t(t * kFBK + k4 + 2 * h);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                Op::pair(lo, hi, a0, a1, e ? bq[q].z : bq[q].x, e ? bq[q].w : bq[q].y);
+                float& av = acc[r][2 * q + e];
+                const float nv = Op::red3(av, lo, hi);
+                if (Op::better(nv, av)) {
+                  const bool first = lo == nv;
+                  pidx[r][2 * q + e] = first ? kg : kg + 1;
+                  av = first ? lo : hi;
+                }
+              }
+            } else {
+              Op::pair(lo, hi, a0, a1, bq[q].x, bq[q].y);
+              acc[r][2 * q] = Op::red3(acc[r][2 * q], lo, hi);
+              Op::pair(lo, hi, a0, a1, bq[q].z, bq[q].w);
+              acc[r][2 * q + 1] = Op::red3(acc[r][2 * q + 1], lo, hi);
+            }
           }
         }
       }
     }
-    if (ARGMAX && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
+    if (ARGMAX && !PAIR && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
       // chunk boundary: remember the chunk of each output's latest strict improvement
       const uint16_t chunk = uint16_t(t / tiles_per_chunk);
 #pragma unroll
@@ -391,10 +414,13 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
       const int lc = wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1);
       const int64_t gc = n0 + lc;
       if (gr >= p.m || gc >= p.n) {
-        if (ARGMAX) cid[lr * kFBN + lc] = kNoChunk;   // padding: never resolved
+        if (ARGMAX && !PAIR) cid[lr * kFBN + lc] = kNoChunk;   // padding: never resolved
         continue;
       }
-      if (!ARGMAX) {
+      if (PAIR) {
+        store_c(C, gr * p.ldc + gc, acc[r][c]);
+        IDX[gr * p.ldc + gc] = pidx[r][c];
+      } else if (!ARGMAX) {
         store_c(C, gr * p.ldc + gc, acc[r][c]);
       } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
         store_c(C, gr * p.ldc + gc, acc_init);
@@ -402,7 +428,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
       }
     }
   }
-  if (!ARGMAX) return;
+  if (!ARGMAX || PAIR) return;
 
   // -------------------------------------------- argmax: bucket by chunk
   __syncthreads();
