@@ -175,8 +175,8 @@ def test_empty_m_or_n():
     assert c.shape == (0, 3)
 
 
-def test_unaligned_leading_dimension_uses_exact_path():
-    """lda not a multiple of 4 (a padded buffer): generic kernel, same bits."""
+def test_unaligned_leading_dimension():
+    """lda not a multiple of 4 (a padded buffer): 4-byte staging of A, same bits."""
     rng = np.random.default_rng(4)
     m, k, n = 70, 37, 50
     buf = rng.standard_normal((m, k + 1)).astype(np.float32)
@@ -272,3 +272,24 @@ def test_i64_out_of_range_falls_back_exactly(semi):
         assert same_bits(c, c0)
         if wa:
             assert np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("k", [37, 300, 1001])
+def test_misaligned_base_and_odd_batch_stride(semi, k):
+    """A starting 4 bytes past a 16-byte boundary and odd batch strides."""
+    rng = np.random.default_rng(k)
+    bs, m, n = 3, 150, 140
+    buf = rng.standard_normal(bs * m * k + 1).astype(np.float32)
+    a = buf[1:].reshape(bs, m, k)
+    b = rng.standard_normal((bs, k, n)).astype(np.float32)
+    ta = torch.from_numpy(buf).to(dev())[1:]
+    tb = torch.from_numpy(b).to(dev())
+    c = torch.empty((bs, m, n), device=dev())
+    am = torch.empty((bs, m, n), dtype=torch.int32, device=dev())
+    N.check(N.lib().tg_gemm_strided_batched(N.SEMIRINGS[semi], 0, 0, bs, m, n, k, ta.data_ptr(), k, m * k,
+                                            tb.data_ptr(), n, k * n, c.data_ptr(), n, m * n, am.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    c0, am0 = oracle(semi, np.ascontiguousarray(a), b)
+    assert same_bits(c.cpu().numpy(), c0) and np.array_equal(am.cpu().numpy(), am0)

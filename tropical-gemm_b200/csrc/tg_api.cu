@@ -66,9 +66,7 @@ struct Problem {
 
 bool fast_f32_ok(const Problem& P) {
   const auto& g = P.g;
-  if ((reinterpret_cast<uintptr_t>(g.a) & 15) != 0) return false;
-  if (g.lda % 4 != 0) return false;
-  if (P.batch > 1 && g.sa % 4 != 0) return false;
+  // any A alignment: the kernel switches to 4-byte copies for unaligned rows
   if (g.k >= (int64_t(1) << 31)) return false;
   // argmax: the re-stream ring holds whole chunks of <= 4 k-tiles (1024 chunks)
   if (g.argmax && (g.k + tg::kFBK - 1) / tg::kFBK > int64_t(4) * tg::kFMaxChunks) return false;
@@ -79,35 +77,38 @@ constexpr int64_t kPairMaxK = 512;
 
 template <int S, bool ARGMAX, bool OUTI = false>
 tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
-  auto kern = tg::fast_f32_kernel<S, ARGMAX, OUTI>;
   const size_t smem = ARGMAX ? tg::kFSmemArgmax : tg::kFSmemValues;
-  static bool configured[64] = {false};
-  if (ARGMAX && P.g.k <= kPairMaxK) {   // configure the pair-tracking variant too
-    static bool configured_pair[64] = {false};
-    int d = 0;
-    cudaGetDevice(&d);
-    if (d < 64 && !configured_pair[d]) {
-      cudaError_t e = cudaFuncSetAttribute(tg::fast_f32_kernel<S, ARGMAX, OUTI, true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      if (e != cudaSuccess) return fail(TG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      configured_pair[d] = true;
-    }
+  // variant: argmax by chunk re-stream or by k-pair tracking (short K);
+  // A staged by 16-byte copies when every batch's A rows are 16-byte aligned
+  const bool pair = ARGMAX && P.g.k <= kPairMaxK;
+  const bool avec = (reinterpret_cast<uintptr_t>(P.g.a) & 15) == 0 && P.g.lda % 4 == 0 &&
+                    (P.batch == 1 || P.g.sa % 4 == 0);
+  using KernT = void (*)(tg::GemmArgs, int, int, float);
+  KernT kern;
+  int variant;
+  if constexpr (OUTI) {   // the i32 path stages padded, aligned copies
+    kern = pair ? tg::fast_f32_kernel<S, ARGMAX, OUTI, true> : tg::fast_f32_kernel<S, ARGMAX, OUTI, false>;
+    variant = pair ? 1 : 0;
+  } else {
+    if (pair) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true> : tg::fast_f32_kernel<S, ARGMAX, false, true, false>;
+    else kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, false, true> : tg::fast_f32_kernel<S, ARGMAX, false, false, false>;
+    variant = (pair ? 1 : 0) + (avec ? 0 : 2);
   }
+  static bool configured[64][4] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
+  if (dev < 64 && !configured[dev][variant]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return fail(TG_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured[dev] = true;
+    configured[dev][variant] = true;
   }
   const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
   int tpc = 2;
   const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
                      (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
   while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
-  // Short K: the re-stream costs as much per output as at long K, so track
-  // the argmax per k-pair in registers instead (measured crossover ~K = 512).
-  if (ARGMAX && P.g.k <= kPairMaxK) kern = tg::fast_f32_kernel<S, ARGMAX, OUTI, true>;
+  // (Short K: the re-stream costs as much per output as at long K, so the
+  // argmax is tracked per k-pair in registers instead; crossover ~K = 512.)
   const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;
   const int64_t gy = (P.g.n + tg::kFBN - 1) / tg::kFBN;
   if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");

@@ -139,9 +139,15 @@ struct TileLoader {
   int a_kq, b_kpar;
   uint32_t a_rowmask;   // bit e: row (t>>3) + 32e exists
   bool b_colok;
+  // A rows not 16-byte aligned (lda % 4 != 0 or a misaligned base): 4-byte copies
+  bool a_vec;
+  const float* a_base;  // A + m0 * lda
+  int64_t a_lda, a_rows;
+  uint32_t a_smem;      // stage-0 A base
+  int tid_;
 
   __device__ __forceinline__ TileLoader(const float* A, const float* B, const GemmArgs& p, int64_t m0, int64_t n0,
-                                        int tid, const float* smem_base) {
+                                        int tid, const float* smem_base, bool avec = true) {
     const int ra = tid >> 3;
     a_kq = (tid & 7) * 4;
     a_step = 32 * p.lda;
@@ -157,6 +163,12 @@ struct TileLoader {
     b_src = b_colok ? B + int64_t(b_kpar) * p.ldb + n0 + nn : B;
     k = p.k;
     a_dst = smem_u32(smem_base) + uint32_t((ra * kFApitch + a_kq) * 4);
+    a_vec = avec;
+    a_base = A + m0 * p.lda;
+    a_lda = p.lda;
+    a_rows = p.m - m0;
+    a_smem = smem_u32(smem_base);
+    tid_ = tid;
     b_dst = smem_u32(smem_base + kFAStage) + uint32_t((nn * 2 + b_kpar) * 4);
   }
 
@@ -169,6 +181,17 @@ struct TileLoader {
   __device__ __forceinline__ void load_a_at(uint32_t soff, int64_t kt) const {
     const int64_t k0 = kt * kFBK;
     const bool interior = k0 + kFBK <= k;
+    if (!a_vec) {
+#pragma unroll
+      for (int e = 0; e < (kFBM * kFBK) / kFThreads; ++e) {
+        const int lin = tid_ + e * kFThreads;
+        const int row = lin >> 5, kk = lin & 31;
+        const bool ok = row < a_rows && k0 + kk < k;
+        cp_async4(a_smem + soff + uint32_t((row * kFApitch + kk) * 4), ok ? a_base + row * a_lda + k0 + kk : a_base,
+                  ok ? 4 : 0);
+      }
+      return;
+    }
     {
       const float* src = a_src + k0;
       int bytes = 16;
@@ -284,7 +307,8 @@ __device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
 // improvement the first of the two products that attains it (value bits and
 // index).  ~3 instructions per product instead of ~1, but no re-stream,
 // whose cost per output does not shrink with K.
-template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false>
+// AVEC: A rows are 16-byte aligned (else A is staged by 4-byte copies).
+template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true>
 __global__ void __launch_bounds__(kFThreads, 1)
 fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   using Op = FastOps<S>;
@@ -307,7 +331,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   const int64_t ktiles = (p.k + kFBK - 1) / kFBK;
   const int kvalid_last = int(p.k - (ktiles - 1) * kFBK);
 
-  const TileLoader ldr(A, B, p, m0, n0, tid, smem);
+  const TileLoader ldr(A, B, p, m0, n0, tid, smem, AVEC);
   uint16_t* cid = reinterpret_cast<uint16_t*>(sbytes + kOffCid);
   if (ARGMAX && !PAIR) {
     for (int i = tid; i < kFBM * kFBN; i += kFThreads) cid[i] = kNoChunk;
