@@ -293,3 +293,29 @@ def test_misaligned_base_and_odd_batch_stride(semi, k):
     torch.cuda.synchronize()
     c0, am0 = oracle(semi, np.ascontiguousarray(a), b)
     assert same_bits(c.cpu().numpy(), c0) and np.array_equal(am.cpu().numpy(), am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_zero_sign_of_value_only_results(semi, dtype):
+    """Results that are a signed zero: the value-only fold must give fmax/fmin's
+    sign (max(+0,-0) = +0 and min(+0,-0) = -0 in either order), on tiles where
+    only some outputs are zero and on tiles where none are."""
+    rng = np.random.default_rng(11)
+    m, k, n = 300, 260, 200
+    a = np.abs(rng.standard_normal((m, k))).astype(dtype)
+    b = np.abs(rng.standard_normal((k, n))).astype(dtype)
+    if semi == "maxplus":
+        a, b = -a, -b
+    elif semi == "maxmul":
+        a = -a
+    for arr in (a, b):
+        arr[:150][rng.random(arr[:150].shape) < 0.3] = 0.0
+        arr[:150][rng.random(arr[:150].shape) < 0.3] = -0.0
+    for wa in (False, True):
+        c, am = engine(semi, a, b, wa)
+        c0, am0 = oracle(semi, a, b, wa)
+        assert same_bits(c, c0)
+        assert np.count_nonzero(c0 == 0) > 0
+        if wa:
+            assert np.array_equal(am, am0)

@@ -340,10 +340,9 @@ tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
   }
   if constexpr (std::is_same<T, double>::value) {
     const double z = S == tg::kMaxPlus ? -double(INFINITY) : (S == tg::kMinPlus ? double(INFINITY) : 0.0);
-    // argmax: the wide kernel (strict update, ~1.03x the reference kernel's
-    // rate at 4096^3 and faster at large tiles); value-only: the generic kernel,
-    // whose fmax fold measured faster than the wide kernel's sign-exact select
-    if (am) return launch_wide_f64<S, true>(P, st, z);
+    // the wide kernel: strict update for argmax; value-only a strict select
+    // with a zero-sign re-run (equal to the fmax/fmin fold, about twice its rate)
+    return am ? launch_wide_f64<S, true>(P, st, z) : launch_wide_f64<S, false>(P, st, z);
   }
   if constexpr (std::is_same<T, int64_t>::value) {
     if (P.g.m * P.g.n >= kI32FastMinOutputs) return launch_i64_via_f64<S>(P, st);

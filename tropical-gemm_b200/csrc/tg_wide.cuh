@@ -1,10 +1,11 @@
 // f64 tropical GEMM kernel (also the compute kernel of the i64 path).
 //
-// FP64 has no paired add and no 3-input max, so this kernel keeps the
-// reference's per-product form -- value-only: add/mul then the max/min;
-// argmax: add/mul then the strict compare that moves value and index
-// (crates/tropical-gemm-cuda/kernels/tropical_gemm.cu:645-758) -- and wins on
-// tiling instead: 128x64x16 CTA tiles, 256 threads, 8x4 outputs per thread
+// FP64 has no paired add and no 3-input max, so this kernel keeps one
+// compare per product.  Argmax: add/mul then the strict compare that moves
+// value and index (crates/tropical-gemm-cuda/kernels/tropical_gemm.cu:645-758).
+// Value-only: the same strict select instead of the reference's fmax/fmin
+// (:191-299), which costs about twice as much on sm_100; the results are equal
+// (see the zero-sign re-run below).  It wins on tiling too: 128x64x16 CTA tiles, 256 threads, 8x4 outputs per thread
 // (the reference uses 32x32 tiles and 4x4 per thread), a 3-stage cp.async
 // pipeline, and 16-byte shared-memory fragment loads.  Semantics are the
 // reference's bit for bit (same operations in the same k order per output).
@@ -99,63 +100,88 @@ wide_f64_kernel(GemmArgs p, double acc_init) {
 
   double acc[8][kWTN];
   int32_t idx[ARGMAX ? 8 : 1][ARGMAX ? kWTN : 1];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < kWTN; ++j) {
-      acc[i][j] = acc_init;
-      if (ARGMAX) idx[i][j] = 0;
-    }
 
+  // RED: 0 = strict-compare select (argmax, or a value-only fold whose
+  // result equals the fmax/fmin fold), 1 = the sign-exact select of wide_reduce
+  auto mainloop = [&](auto red_tag) {
+    constexpr int RED = decltype(red_tag)::value;
 #pragma unroll
-  for (int s = 0; s < kWStages - 1; ++s) {
-    if (s < ktiles) load(s, s);
-    cp_async_commit();
-  }
-  for (int64_t t = 0; t < ktiles; ++t) {
-    cp_async_wait<kWStages - 2>();
-    __syncthreads();
-    {
-      const int64_t nt = t + kWStages - 1;
-      if (nt < ktiles) load(int(nt % kWStages), nt);
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < kWTN; ++j) {
+        acc[i][j] = acc_init;
+        if (ARGMAX) idx[i][j] = 0;
+      }
+#pragma unroll
+    for (int s = 0; s < kWStages - 1; ++s) {
+      if (s < ktiles) load(s, s);
       cp_async_commit();
     }
-    const double* As = wsm + (t % kWStages) * kWStage;
-    const double* Bs = As + kWBK * kWApitch;
-    const int kcount = int((p.k - t * kWBK) < kWBK ? (p.k - t * kWBK) : kWBK);
-    const int32_t kbase = int32_t(t * kWBK);
-    auto step = [&](int kk) {
-      double av[8], bv[kWTN];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const double2 a2 = *reinterpret_cast<const double2*>(As + kk * kWApitch + 2 * ty + 32 * q);
-        av[2 * q] = a2.x; av[2 * q + 1] = a2.y;
+    for (int64_t t = 0; t < ktiles; ++t) {
+      cp_async_wait<kWStages - 2>();
+      __syncthreads();
+      {
+        const int64_t nt = t + kWStages - 1;
+        if (nt < ktiles) load(int(nt % kWStages), nt);
+        cp_async_commit();
       }
+      const double* As = wsm + (t % kWStages) * kWStage;
+      const double* Bs = As + kWBK * kWApitch;
+      const int kcount = int((p.k - t * kWBK) < kWBK ? (p.k - t * kWBK) : kWBK);
+      const int32_t kbase = int32_t(t * kWBK);
+      auto step = [&](int kk) {
+        double av[8], bv[kWTN];
 #pragma unroll
-      for (int q = 0; q < kWTN / 2; ++q) {
-        const double2 b2 = *reinterpret_cast<const double2*>(Bs + kk * kWBpitch + 2 * tx + 32 * q);
-        bv[2 * q] = b2.x; bv[2 * q + 1] = b2.y;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < kWTN; ++j) {
-          const double prod = R::mul(av[i], bv[j]);
-          if (ARGMAX) {
-            if (R::better(prod, acc[i][j])) { acc[i][j] = prod; idx[i][j] = kbase + kk; }
-          } else {
-            acc[i][j] = wide_reduce<S>(acc[i][j], prod);
-          }
+        for (int q = 0; q < 4; ++q) {
+          const double2 a2 = *reinterpret_cast<const double2*>(As + kk * kWApitch + 2 * ty + 32 * q);
+          av[2 * q] = a2.x; av[2 * q + 1] = a2.y;
         }
-    };
-    if (kcount == kWBK) {
 #pragma unroll
-      for (int kk = 0; kk < kWBK; ++kk) step(kk);
-    } else {
-      for (int kk = 0; kk < kcount; ++kk) step(kk);
+        for (int q = 0; q < kWTN / 2; ++q) {
+          const double2 b2 = *reinterpret_cast<const double2*>(Bs + kk * kWBpitch + 2 * tx + 32 * q);
+          bv[2 * q] = b2.x; bv[2 * q + 1] = b2.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < kWTN; ++j) {
+            const double prod = R::mul(av[i], bv[j]);
+            if (ARGMAX) {
+              if (R::better(prod, acc[i][j])) { acc[i][j] = prod; idx[i][j] = kbase + kk; }
+            } else if (RED == 0) {
+              if (R::better(prod, acc[i][j])) acc[i][j] = prod;
+            } else {
+              acc[i][j] = wide_reduce<S>(acc[i][j], prod);
+            }
+          }
+      };
+      if (kcount == kWBK) {
+#pragma unroll
+        for (int kk = 0; kk < kWBK; ++kk) step(kk);
+      } else {
+        for (int kk = 0; kk < kcount; ++kk) step(kk);
+      }
+    }
+    cp_async_wait<0>();
+  };
+
+  mainloop(std::integral_constant<int, 0>{});
+  // Value-only f64 MaxPlus/MinPlus: the strict select equals the fmax/fmin
+  // fold except for the sign of a zero result (fmax(-0, +0) = +0 in either
+  // order, the select keeps the first zero seen).  A CTA with any zero result
+  // re-runs its tile with the sign-exact select; MaxMul (accumulator starts
+  // at +0 and never decreases) and integer outputs need no re-run.
+  if constexpr (!ARGMAX && !OUTI && S != kMaxMul) {
+    int zero = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < kWTN; ++j) zero |= (acc[i][j] == 0.0);
+    if (__syncthreads_or(zero)) {
+      __syncthreads();
+      mainloop(std::integral_constant<int, 1>{});
     }
   }
-  cp_async_wait<0>();
 
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
