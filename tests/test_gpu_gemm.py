@@ -319,3 +319,30 @@ def test_zero_sign_of_value_only_results(semi, dtype):
         assert np.count_nonzero(c0 == 0) > 0
         if wa:
             assert np.array_equal(am, am0)
+
+
+def test_i32_argmax_beyond_the_chunk_limit():
+    """i32 with argmax and K past the fast kernel's chunk table (4 x 1024 tiles
+    of 32): both the allocating entry point and tg_gemm_i32_noalloc must fall
+    back to the exact kernel, not run the fast kernel with oversized chunks."""
+    import ctypes
+    rng = np.random.default_rng(12)
+    k = 4 * 1024 * 32 + 5000
+    for m, n, noalloc in ((128, 128, False), (40, 48, True)):
+        a = rng.integers(-50, 50, (m, k)).astype(np.int32)
+        b = rng.integers(-50, 50, (k, n)).astype(np.int32)
+        c0, am0 = oracle("maxplus", a, b)
+        if not noalloc:
+            c, am = engine("maxplus", a, b)
+        else:
+            L = N.lib()
+            i64, vp, i32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
+            L.tg_gemm_i32_noalloc.argtypes = [i32, i32, i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, vp]
+            L.tg_gemm_i32_noalloc.restype = i32
+            ta, tb = torch.from_numpy(a).to(dev()), torch.from_numpy(b).to(dev())
+            tc = torch.empty((m, n), dtype=torch.int32, device=dev())
+            ti = torch.empty((m, n), dtype=torch.int32, device=dev())
+            N.check(L.tg_gemm_i32_noalloc(0, 0, m, n, k, ta.data_ptr(), k, tb.data_ptr(), n, tc.data_ptr(), n,
+                                          ti.data_ptr(), torch.cuda.current_stream().cuda_stream))
+            c, am = tc.cpu().numpy(), ti.cpu().numpy()
+        assert np.array_equal(c, c0) and np.array_equal(am, am0)

@@ -336,7 +336,7 @@ tg_status dispatch_typed(const Problem& P, cudaStream_t st) {
     if (fast_f32_ok(P)) return am ? launch_fast_f32<S, true>(P, st, z) : launch_fast_f32<S, false>(P, st, z);
   }
   if constexpr (std::is_same<T, int32_t>::value) {
-    if (P.g.m * P.g.n >= kI32FastMinOutputs) return launch_i32_via_f32<S>(P, st);
+    if (P.g.m * P.g.n >= kI32FastMinOutputs && fast_f32_ok(P)) return launch_i32_via_f32<S>(P, st);
   }
   if constexpr (std::is_same<T, double>::value) {
     const double z = S == tg::kMaxPlus ? -double(INFINITY) : (S == tg::kMinPlus ? double(INFINITY) : 0.0);
@@ -631,7 +631,7 @@ extern "C" tg_status tg_gemm_i32_noalloc(tg_semiring semiring, tg_layout layout,
   P.g = row ? tg::GemmArgs{m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, argmax}
             : tg::GemmArgs{n, m, k, b, ldb, 0, a, lda, 0, c, ldc, 0, argmax};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (k == 0) {   // no scratch needed: semiring zero and index 0
+  if (k == 0 || !fast_f32_ok(P)) {   // no scratch needed: semiring zero and index 0, or the exact kernel
     switch (semiring) {
       case TG_MAXPLUS: return dispatch_typed<tg::kMaxPlus, int32_t>(P, st);
       case TG_MINPLUS: return dispatch_typed<tg::kMinPlus, int32_t>(P, st);
