@@ -49,17 +49,29 @@ constexpr size_t kFSmemValues = size_t(kFStages) * kFStageFloats * 4;
 // Argmax kernel shared-memory map.  During the k loop: the three pipeline
 // stages and one chunk id (u16) per CTA output.  After the outputs are
 // bucketed by chunk, kRStages ring slots (overlaying stages and chunk ids)
-// re-stream the owned chunks; the bucketed list and offsets sit above.
-constexpr int kRStages = 5;
-constexpr int kRBpitch = kFBN + 4;                         // padded B rows: column reads spread over banks
-constexpr int kRStageFloats = kFAStage + kFBK * kRBpitch;  // one ring slot
+// re-stream the owned chunks -- three two-tile chunks resident or in flight,
+// so the scan of one chunk overlaps the copies of the next two; the bucketed
+// list and its u16 offsets sit above the ring.
+constexpr int kRStages = 6;
+constexpr int kRAFloats = kFBM * kFBK;                     // A slot: 128 rows x 32 k, 16-byte groups swizzled
+constexpr int kRStageFloats = kRAFloats + kFBK * kFBN;     // + B slot: 32 k x 128 n, swizzled
 constexpr size_t kOffCid = kFSmemValues;
 constexpr size_t kOffList = size_t(kRStages) * kRStageFloats * 4;
 constexpr size_t kOffOff = kOffList + size_t(kFBM * kFBN) * 2;
-constexpr size_t kFSmemArgmax = kOffOff + size_t(kFMaxChunks + 1) * 4;
+constexpr size_t kFSmemArgmax = kOffOff + size_t(kFMaxChunks + 1) * 2;
 static_assert(kOffCid + size_t(kFBM * kFBN) * 2 <= kOffList, "chunk ids overlap the list");
-static_assert(kFSmemArgmax <= 227 * 1024, "argmax kernel exceeds shared memory");
-static_assert((kRStageFloats * 4) % 16 == 0 && (kRBpitch * 4) % 16 == 0, "ring alignment");
+static_assert(size_t(2 * (kFMaxChunks + 1)) * 4 <= kOffCid, "bucket counters overlap the chunk ids");
+static_assert(kFSmemArgmax <= 232448, "argmax kernel exceeds shared memory");
+static_assert(kFBM * kFBN <= 65535, "u16 bucket offsets");
+
+// Ring-slot element positions.  Rows keep their natural length (no padding);
+// instead the 16-byte groups of a row are XOR-swizzled by the row index, so
+// the scan's column reads (4 lanes on consecutive k of one output, 8 outputs
+// per warp) spread over the banks.
+__device__ __forceinline__ int ring_a(int r, int k) { return r * kFBK + ((((k >> 2) ^ (r & 7)) << 2) | (k & 3)); }
+__device__ __forceinline__ int ring_b(int k, int n) {
+  return kRAFloats + k * kFBN + ((((n >> 2) ^ (k & 7)) << 2) | (n & 3));
+}
 
 template <int S> struct FastOps;
 template <> struct FastOps<kMaxPlus> {
@@ -232,49 +244,57 @@ struct TileLoader {
   }
 };
 
-// Re-stream staging into a ring slot: A exactly as in the k loop, B in its
-// natural [k][n] layout with padded rows (the scan reads single columns, so
-// the k-pair interleave is not needed).  16-byte copies when B rows are
-// 16-byte aligned, 4-byte copies otherwise.
-struct RestreamLoader {
-  const TileLoader* main;
-  const float* B;
-  int64_t n0, kdim, ndim, ldb;
+// Re-stream staging of one k-tile into a ring slot (layout of ring_a /
+// ring_b).  16-byte copies when rows are 16-byte aligned, 4-byte copies
+// otherwise; out-of-range elements are zero-filled (the scan masks k >= K).
+struct RingLoader {
+  const float* A;   // row m0 of this batch's A
+  const float* B;   // this batch's B
+  int64_t rows, cols, kdim, lda, ldb, n0;
   int tid;
-  bool b_vec;
+  bool a_vec, b_vec;
   uint32_t base;
-  __device__ __forceinline__ RestreamLoader(const TileLoader* ml, const float* B_, const GemmArgs& p, int64_t n0_,
-                                            int tid_, const float* smem_base, bool vec)
-      : main(ml), B(B_), n0(n0_), kdim(p.k), ndim(p.n), ldb(p.ldb), tid(tid_), b_vec(vec),
-        base(smem_u32(smem_base)) {}
+  __device__ __forceinline__ RingLoader(const float* A_, const float* B_, const GemmArgs& p, int64_t m0, int64_t n0_,
+                                        int tid_, const float* smem_base, bool avec, bool bvec)
+      : A(A_ + m0 * p.lda), B(B_), rows(p.m - m0), cols(p.n - n0_), kdim(p.k), lda(p.lda), ldb(p.ldb), n0(n0_),
+        tid(tid_), a_vec(avec), b_vec(bvec), base(smem_u32(smem_base)) {}
   __device__ __forceinline__ void load(int slot, int64_t kt) const {
-    const uint32_t soff = uint32_t(slot) * uint32_t(kRStageFloats * 4);
-    main->load_a_at(soff, kt);
-    const uint32_t bbase = base + soff + uint32_t(kFAStage * 4);
+    const uint32_t sb = base + uint32_t(slot) * uint32_t(kRStageFloats * 4);
     const int64_t k0 = kt * kFBK;
-    if (b_vec) {
+    if (a_vec) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int q = tid + e * kFThreads;
-        const int kk = q >> 5, c4 = (q & 31) * 4;
-        const int64_t gk = k0 + kk, gc = n0 + c4;
-        int bytes = 0;
-        const float* src = B;
-        if (gk < kdim && gc < ndim) {
-          const int64_t rem = ndim - gc;
-          bytes = rem >= 4 ? 16 : int(rem) * 4;
-          src = B + gk * ldb + gc;
-        }
-        cp_async16(bbase + uint32_t((kk * kRBpitch + c4) * 4), src, bytes);
+      for (int e = 0; e < (kFBM * kFBK / 4) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int r = lin >> 3, kq = (lin & 7) * 4;
+        const int64_t rem = kdim - (k0 + kq);
+        const int bytes = r < rows ? (rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0)) : 0;
+        cp_async16(sb + uint32_t(ring_a(r, kq) * 4), bytes ? A + r * lda + k0 + kq : A, bytes);
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int q = tid + e * kFThreads;
-        const int kk = q >> 7, c = q & 127;
-        const int64_t gk = k0 + kk, gc = n0 + c;
-        const bool ok = gk < kdim && gc < ndim;
-        cp_async4(bbase + uint32_t((kk * kRBpitch + c) * 4), ok ? B + gk * ldb + gc : B, ok ? 4 : 0);
+      for (int e = 0; e < (kFBM * kFBK) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int r = lin >> 5, kk = lin & 31;
+        const bool ok = r < rows && k0 + kk < kdim;
+        cp_async4(sb + uint32_t(ring_a(r, kk) * 4), ok ? A + r * lda + k0 + kk : A, ok ? 4 : 0);
+      }
+    }
+    if (b_vec) {
+#pragma unroll
+      for (int e = 0; e < (kFBK * kFBN / 4) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int kk = lin >> 5, c = (lin & 31) * 4;
+        const int64_t rem = cols - c;
+        const int bytes = k0 + kk < kdim ? (rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0)) : 0;
+        cp_async16(sb + uint32_t(ring_b(kk, c) * 4), bytes ? B + (k0 + kk) * ldb + n0 + c : B, bytes);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < (kFBK * kFBN) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int kk = lin >> 7, c = lin & 127;
+        const bool ok = k0 + kk < kdim && c < cols;
+        cp_async4(sb + uint32_t(ring_b(kk, c) * 4), ok ? B + (k0 + kk) * ldb + n0 + c : B, ok ? 4 : 0);
       }
     }
   }
@@ -458,32 +478,36 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   __syncthreads();
   TG_PHASE(2);
   uint16_t* list = reinterpret_cast<uint16_t*>(sbytes + kOffList);
-  int* off = reinterpret_cast<int*>(sbytes + kOffOff);
+  uint16_t* off = reinterpret_cast<uint16_t*>(sbytes + kOffOff);
+  int* cnt = reinterpret_cast<int*>(smem);            // the stages are idle after the k loop
+  int* cursor = cnt + (kFMaxChunks + 1);
   const int nchunks = int((ktiles + tiles_per_chunk - 1) / tiles_per_chunk);
-  for (int i = tid; i <= nchunks; i += kFThreads) off[i] = 0;
+  for (int i = tid; i <= nchunks; i += kFThreads) cnt[i] = 0;
   __syncthreads();
   for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
     const uint16_t ch = cid[i];
-    if (ch != kNoChunk) atomicAdd(&off[ch + 1], 1);
+    if (ch != kNoChunk) atomicAdd(&cnt[ch + 1], 1);
   }
   __syncthreads();
   if (warp == 0) {  // inclusive scan of counts: bucket c is list[off[c], off[c+1])
     int carry = 0;
     for (int base = 1; base <= nchunks; base += 32) {
       int i = base + lane;
-      int v = i <= nchunks ? off[i] : 0;
+      int v = i <= nchunks ? cnt[i] : 0;
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
         int u = __shfl_up_sync(0xffffffffu, v, d);
         if (lane >= d) v += u;
       }
-      if (i <= nchunks) off[i] = v + carry;
+      if (i <= nchunks) cnt[i] = v + carry;
       carry += __shfl_sync(0xffffffffu, v, 31);
     }
   }
   __syncthreads();
-  int* cursor = reinterpret_cast<int*>(smem);   // stage 0 is idle here
-  for (int i = tid; i < nchunks; i += kFThreads) cursor[i] = off[i];
+  for (int i = tid; i <= nchunks; i += kFThreads) {
+    off[i] = uint16_t(cnt[i]);
+    if (i < nchunks) cursor[i] = cnt[i];
+  }
   __syncthreads();
   for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
     const uint16_t ch = cid[i];
@@ -495,10 +519,10 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   // Every output of chunk c had its last strict improvement in c, so its
   // final value is the max (min) of its products over c, and its reference
   // index is the first k of c whose product equals that value.  Tiles of the
-  // owned chunks stream through a kRStages-deep ring (the chunk ids are dead
-  // now); a chunk is scanned once all its tiles have landed.
+  // owned chunks stream through a kRStages-deep ring (the chunk ids and the
+  // counters are dead now); a chunk is scanned once all its tiles have landed.
   TG_PHASE(3);
-  const RestreamLoader rl(&ldr, B, p, n0, tid, smem, b_vec != 0);
+  const RingLoader rl(A, B, p, m0, n0, tid, smem, AVEC, b_vec != 0);
   auto next_owned = [&](int c) {
     while (c < nchunks && off[c + 1] == off[c]) ++c;
     return c;
@@ -540,17 +564,17 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
     issue_until(seq0 + kRStages);
     const int beg = off[c], end = off[c + 1];
     const int slot0 = int(seq0 % kRStages);
-    const int klast = int(p.k - (t0 + nt - 1) * kFBK);   // valid k in the chunk's last tile
+    const int klast = int(i64min(kFBK, p.k - (t0 + nt - 1) * kFBK));   // valid k in the chunk's last tile
     // 64 groups of 4 lanes; lane `sub` owns k = sub, sub+4, ..., sub+28 of
-    // every tile of the chunk (column reads spread over banks).  Pass 1: group
-    // max of the products; pass 2: lowest k whose product equals it.  Trip
-    // counts are block-uniform, so every lane reaches the shuffles.
-    // Each group handles two entries per round (independent chains for ILP);
-    // the products of pass 1 stay in registers for pass 2.
+    // every tile of the chunk.  Pass 1: group max of the products; pass 2:
+    // lowest k whose product equals it.  Trip counts are block-uniform, so
+    // every lane reaches the shuffles.  Each group handles two entries per
+    // round (independent chains for ILP); the products of pass 1 stay in
+    // registers for pass 2.
     if (nt == 2 && klast == kFBK) {
-      // Full two-tile chunk (every chunk but possibly the last): no k-range
-      // masks; pass 1 is a max3 tree, pass 2 a 16-bit equality mask whose
-      // lowest set bit is the lane's first winning k (bit order = k order).
+      // Full two-tile chunk: no k-range masks; pass 1 is a max3 tree, pass 2
+      // a 16-bit equality mask whose lowest set bit is the lane's first
+      // winning k (bit order = k order).
       const float* st0 = smem + slot0 * kRStageFloats;
       const float* st1 = smem + (slot0 + 1 >= kRStages ? slot0 + 1 - kRStages : slot0 + 1) * kRStageFloats;
       for (int e0 = beg; e0 < end; e0 += 2 * (kFThreads / 4)) {
@@ -563,8 +587,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
           float pv[16];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            pv[i] = Op::mul(st0[lr * kFApitch + sub + 4 * i], st0[kFAStage + (sub + 4 * i) * kRBpitch + lc]);
-            pv[8 + i] = Op::mul(st1[lr * kFApitch + sub + 4 * i], st1[kFAStage + (sub + 4 * i) * kRBpitch + lc]);
+            pv[i] = Op::mul(st0[ring_a(lr, sub + 4 * i)], st0[ring_b(sub + 4 * i, lc)]);
+            pv[8 + i] = Op::mul(st1[ring_a(lr, sub + 4 * i)], st1[ring_b(sub + 4 * i, lc)]);
           }
           float m = Op::red3(Op::red3(Op::red3(pv[0], pv[1], pv[2]), Op::red3(pv[3], pv[4], pv[5]),
                                       Op::red3(pv[6], pv[7], pv[8])),
@@ -587,7 +611,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
           if (act && first != 0xFFFFFFFFu && kf == first) {
             const float* st = first >= unsigned(kFBK) ? st1 : st0;
             const int kk = int(first) & (kFBK - 1);
-            const float v = Op::mul(st[lr * kFApitch + kk], st[kFAStage + kk * kRBpitch + lc]);
+            const float v = Op::mul(st[ring_a(lr, kk)], st[ring_b(kk, lc)]);
             const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
             store_c(C, gofs, v);
             IDX[gofs] = int32_t(t0 * kFBK + first);
@@ -618,11 +642,10 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
           const int kc = j == nt - 1 ? klast : kFBK;
 #pragma unroll
           for (int u = 0; u < kE; ++u) {
-            const float* arow = st + (o[u] >> 7) * kFApitch + sub;
-            const float* bcol = st + kFAStage + sub * kRBpitch + (o[u] & 127);
+            const int lr = o[u] >> 7, lc = o[u] & 127;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              pr[u][j][i] = Op::mul(arow[4 * i], bcol[4 * i * kRBpitch]);
+              pr[u][j][i] = Op::mul(st[ring_a(lr, sub + 4 * i)], st[ring_b(sub + 4 * i, lc)]);
               if (sub + 4 * i < kc && Op::better(pr[u][j][i], best[u])) best[u] = pr[u][j][i];
             }
           }
