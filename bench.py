@@ -195,6 +195,65 @@ def extras(dev):
     return res
 
 
+CASES = ("backward", "f64", "f64_values", "apsp_step", "minplus_inf")
+
+
+def run_case(args):
+    """One secondary workload, timed alone (CUDA events, `--steps` launches after
+    `--warmup`), for per-kernel numbers and ncu captures; prints one JSON line.
+    Not the driver's bench line (that is the default mode)."""
+    from tropical_gemm import _native as Nat
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(1)
+    out = {"case": args.case, "steps": args.steps, "warmup": args.warmup}
+    if args.case == "backward":
+        # BASELINE config 3 shapes: grad_A and grad_B of a batch of 64 [512x256].[256x512]
+        bs, m, k, n = 64, 512, 256, 512
+        a = torch.from_numpy(rng.standard_normal((bs, m, k), dtype=np.float32)).to(dev)
+        b = torch.from_numpy(rng.standard_normal((bs, k, n), dtype=np.float32)).to(dev)
+        _, am = Nat.gemm_batched("maxplus", a, b, True)
+        gc = torch.ones((bs, m, n), dtype=torch.float32, device=dev)
+
+        def step():
+            Nat.backward("maxplus", True, gc, am, k)
+            Nat.backward("maxplus", False, gc, am, k)
+
+        ms = _time_ms(step, reps=args.steps, warm=args.warmup)
+        # per gradient: read grad_C (4 B) + argmax (4 B) per output, write the gradient once
+        alg = 2 * bs * m * n * 8 + bs * (m * k + k * n) * 4
+        out.update({"ms": ms, "algorithmic_bytes": alg, "gbs": alg / (ms * 1e-3) / 1e9,
+                    "config": {"batch": bs, "m": m, "k": k, "n": n, "dtype": "f32"}})
+    elif args.case in ("f64", "f64_values"):
+        sz = args.size if args.size != 8192 else 4096
+        a = torch.rand((sz, sz), dtype=torch.float64, device=dev)
+        b = torch.rand((sz, sz), dtype=torch.float64, device=dev)
+        wa = args.case == "f64"
+        ms = _time_ms(lambda: Nat.gemm("maxplus", a, b, wa), reps=args.steps, warm=args.warmup)
+        out.update({"ms": ms, "ops_per_s": float(sz) ** 3 / (ms * 1e-3),
+                    "config": {"m": sz, "n": sz, "k": sz, "dtype": "f64", "argmax": wa}})
+    elif args.case == "apsp_step":
+        n = args.size
+        mask = rng.random((n, n)) < 0.05
+        d = np.where(mask, rng.integers(1, 1001, (n, n)), 46340).astype(np.int32)
+        np.fill_diagonal(d, 0)
+        td = torch.from_numpy(d).to(dev)
+        ms = _time_ms(lambda: Nat.gemm("minplus", td, td, True), reps=args.steps, warm=args.warmup)
+        out.update({"ms": ms, "ops_per_s": float(n) ** 3 / (ms * 1e-3),
+                    "config": {"n": n, "dtype": "i32", "density": 0.05, "argmax": True}})
+    elif args.case == "minplus_inf":
+        n = args.size
+        mats = []
+        for _ in range(2):
+            v = (100 * rng.random((n, n))).astype(np.float32)
+            v[rng.random((n, n)) < 0.9] = np.inf
+            mats.append(torch.from_numpy(v).to(dev))
+        ms = _time_ms(lambda: Nat.gemm("minplus", mats[0], mats[1], True), reps=args.steps, warm=args.warmup)
+        out.update({"ms": ms, "ops_per_s": float(n) ** 3 / (ms * 1e-3),
+                    "config": {"n": n, "dtype": "f32", "inf_fraction": 0.9, "argmax": True}})
+    print(json.dumps(out), flush=True)
+
+
 def dist_setup(n_gpus: int):
     if n_gpus > 1 or "RANK" in os.environ:
         import torch.distributed as dist
@@ -440,7 +499,11 @@ def main():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-extras", action="store_true", help="skip the other BASELINE configs (extra keys)")
     p.add_argument("--size", type=int, default=8192, help="square size (8192 = BASELINE config 2a)")
+    p.add_argument("--case", choices=CASES, help="time one secondary workload alone (for profiling)")
     args = p.parse_args()
+    if args.case:
+        run_case(args)
+        return
     global M, N_, K
     M = N_ = K = args.size
     if args.impl == "reference":

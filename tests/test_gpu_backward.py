@@ -23,7 +23,7 @@ def _close(x, y, rtol=RTOL):
 
 @pytest.mark.parametrize("semi", ["maxplus", "minplus", "maxmul"])
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
-@pytest.mark.parametrize("shape", [(5, 7, 3), (64, 300, 129), (300, 40, 257), (33, 2000, 65)])
+@pytest.mark.parametrize("shape", [(5, 7, 3), (64, 300, 129), (300, 40, 257), (33, 2000, 65), (96, 256, 128), (40, 3000, 64)])
 def test_backward_matches_oracle(semi, dtype, shape):
     m, k, n = shape
     rng = np.random.default_rng(m * k + n)

@@ -421,7 +421,17 @@ tg_status hist_launch(bool rows_kind, const tg::HistArgs& h, int64_t batch, cuda
     g.arg = h.arg + b0 * h.sc;
     if (h.w) g.w = static_cast<const T*>(h.w) + b0 * h.sw;
     g.out = static_cast<T*>(h.out) + b0 * h.so;
-    if (bins <= size_t(max_optin) && (rows_kind ? h.rows <= 0x7fffffff : (h.cols + 31) / 32 <= 0x7fffffff)) {
+    const size_t wbins = size_t(h.k) * sizeof(T) * 8;   // one warp per row, 8 rows per CTA
+    if (rows_kind && wbins <= size_t(max_optin) && (h.rows + 7) / 8 <= 0x7fffffff) {
+      constexpr int64_t epv = 16 / sizeof(T);
+      // 16-byte grad_C loads (and 4 * epv-byte argmax loads) on every row
+      const bool vec = (reinterpret_cast<uintptr_t>(g.gc) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(g.arg) & (4 * epv - 1)) == 0 && h.cols % epv == 0 &&
+                       h.ldc % epv == 0 && (nb == 1 || h.sc % epv == 0);
+      auto kern = vec ? tg::hist_rows_warp_kernel<T, true> : tg::hist_rows_warp_kernel<T, false>;
+      if (wbins > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(wbins));
+      kern<<<dim3(unsigned((h.rows + 7) / 8), unsigned(nb)), 256, wbins, st>>>(g);
+    } else if (bins <= size_t(max_optin) && (rows_kind ? h.rows <= 0x7fffffff : (h.cols + 31) / 32 <= 0x7fffffff)) {
       if (rows_kind) {
         auto kern = tg::hist_rows_kernel<T>;
         if (bins > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bins));

@@ -7,9 +7,10 @@
 // multiplicative MaxMul rule :521-548).
 //
 // B200 design: both gradients are histograms of grad_C keyed by argmax.
-//  * grad_A (row histogram): one CTA per C row accumulates K bins in shared
-//    memory and writes the whole grad_A row once, coalesced -- no global
-//    atomics and no separate zero-fill pass.
+//  * grad_A (row histogram): one warp per C row accumulates K bins in shared
+//    memory (16-byte loads of grad_C and argmax) and writes the whole grad_A
+//    row once, coalesced -- no global atomics and no separate zero-fill
+//    pass.  K too large for 8 warps' bins: one CTA per row shares them.
 //  * grad_B (column histogram): one CTA per 32-column strip walks every
 //    row of the strip with coalesced loads, accumulates K x 32 bins in
 //    shared memory, then writes its grad_B strip once.
@@ -58,8 +59,50 @@ __global__ void __launch_bounds__(256) hist_rows_kernel(HistArgs p) {
     out[i] = p.accumulate ? out[i] + bins[i] : bins[i];
 }
 
+// Same histogram with one warp per C row: 8 rows per CTA, K bins per warp
+// (no CTA barrier), and VEC = 16-byte loads of grad_C and argmax (EPV
+// elements per lane per step) when every row is 16-byte aligned.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) hist_rows_warp_kernel(HistArgs p) {
+  extern __shared__ __align__(16) unsigned char hsm[];
+  constexpr int EPV = 16 / sizeof(T);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = int64_t(blockIdx.x) * 8 + warp, batch = blockIdx.y;
+  if (r >= p.rows) return;   // warp-level work only below
+  T* bins = reinterpret_cast<T*>(hsm) + int64_t(warp) * p.k;
+  const T* gc = static_cast<const T*>(p.gc) + batch * p.sc + r * p.ldc;
+  const int32_t* arg = p.arg + batch * p.sc + r * p.ldc;
+  const T* w = p.w ? static_cast<const T*>(p.w) + batch * p.sw : nullptr;
+  T* out = static_cast<T*>(p.out) + batch * p.so + r * p.ldo;
+  for (int64_t i = lane; i < p.k; i += 32) bins[i] = T(0);
+  __syncwarp();
+  auto add = [&](int32_t kk, T g, int64_t c) {
+    if (kk < 0 || kk >= p.k) return;
+    if (w) g = g * w[int64_t(kk) * p.ldw + c];
+    atomicAdd(&bins[kk], g);
+  };
+  if constexpr (VEC) {
+    for (int64_t c = int64_t(lane) * EPV; c < p.cols; c += 32 * EPV) {
+      if constexpr (EPV == 4) {
+        const int4 a4 = *reinterpret_cast<const int4*>(arg + c);
+        const float4 g4 = *reinterpret_cast<const float4*>(gc + c);
+        add(a4.x, g4.x, c); add(a4.y, g4.y, c + 1); add(a4.z, g4.z, c + 2); add(a4.w, g4.w, c + 3);
+      } else {
+        const int2 a2 = *reinterpret_cast<const int2*>(arg + c);
+        const double2 g2 = *reinterpret_cast<const double2*>(gc + c);
+        add(a2.x, g2.x, c); add(a2.y, g2.y, c + 1);
+      }
+    }
+  } else {
+    for (int64_t c = lane; c < p.cols; c += 32) add(arg[c], gc[c], c);
+  }
+  __syncwarp();
+  for (int64_t i = lane; i < p.k; i += 32) out[i] = p.accumulate ? out[i] + bins[i] : bins[i];
+}
+
 // grad_out[k, c] (+)= sum_r [arg[r,c] == k] * gc[r,c] * (w ? w[r*ldw + k] : 1)
-// One CTA per 32-column strip; 256 threads = 8 row lanes x 32 columns.
+// One CTA per 32-column strip; 256 threads = 8 row lanes x 32 columns, four
+// rows per lane in flight.
 template <typename T>
 __global__ void __launch_bounds__(256) hist_cols_kernel(HistArgs p) {
   extern __shared__ __align__(16) unsigned char hsm[];
@@ -74,7 +117,24 @@ __global__ void __launch_bounds__(256) hist_cols_kernel(HistArgs p) {
   __syncthreads();
   const int64_t c = c0 + lane;
   if (c < p.cols) {
-    for (int64_t r = rl; r < p.rows; r += 8) {
+    int64_t r = rl;
+    for (; r + 24 < p.rows; r += 32) {
+      int32_t kk[4];
+      T g[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        kk[u] = arg[(r + 8 * u) * p.ldc + c];
+        g[u] = gc[(r + 8 * u) * p.ldc + c];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (kk[u] < 0 || kk[u] >= p.k) continue;
+        T v = g[u];
+        if (w) v = v * w[(r + 8 * u) * p.ldw + kk[u]];
+        atomicAdd(&bins[int64_t(kk[u]) * 32 + lane], v);
+      }
+    }
+    for (; r < p.rows; r += 8) {
       const int32_t kk = arg[r * p.ldc + c];
       if (kk < 0 || kk >= p.k) continue;
       T g = gc[r * p.ldc + c];
