@@ -366,7 +366,11 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
     for (int c = 0; c < 8; ++c) {
       acc[r][c] = acc_init;
       if (ARGMAX && !PAIR) snap[r][c] = acc_init;
+#ifdef TG_PAIR_EAGER
       if (PAIR) pidx[r][c] = 0;
+#else
+      if (PAIR) pidx[r][c] = -1;
+#endif
     }
 
   // ------------------------------------------------------------ main loop
@@ -416,11 +420,16 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
                 Op::pair(lo, hi, a0, a1, e ? bq[q].z : bq[q].x, e ? bq[q].w : bq[q].y);
                 float& av = acc[r][2 * q + e];
                 const float nv = Op::red3(av, lo, hi);
+#ifdef TG_PAIR_EAGER
                 if (Op::better(nv, av)) {
                   const bool first = lo == nv;
                   pidx[r][2 * q + e] = first ? kg : kg + 1;
                   av = first ? lo : hi;
                 }
+#else
+                if (Op::better(nv, av)) pidx[r][2 * q + e] = kg;
+                av = nv;
+#endif
               }
             } else {
               Op::pair(lo, hi, a0, a1, bq[q].x, bq[q].y);
@@ -462,8 +471,30 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
         continue;
       }
       if (PAIR) {
+#ifdef TG_PAIR_EAGER
         store_c(C, gr * p.ldc + gc, acc[r][c]);
         IDX[gr * p.ldc + gc] = pidx[r][c];
+#else
+        // pidx: first k of the pair that held the last strict improvement
+        // (-1: none, the output is (zero, 0)).  The reference's index is the
+        // pair's first k whose product equals the final value; its bits are
+        // that product's (the fold may differ in the sign of a zero).
+        const int32_t kg = pidx[r][c];
+        float v = acc_init;
+        int32_t kw = 0;
+        if (kg >= 0) {
+          const float lo = Op::mul(A[gr * p.lda + kg], B[int64_t(kg) * p.ldb + gc]);
+          if (lo == acc[r][c] || kg + 1 >= p.k) {
+            v = lo;
+            kw = kg;
+          } else {
+            v = Op::mul(A[gr * p.lda + kg + 1], B[int64_t(kg + 1) * p.ldb + gc]);
+            kw = kg + 1;
+          }
+        }
+        store_c(C, gr * p.ldc + gc, v);
+        IDX[gr * p.ldc + gc] = kw;
+#endif
       } else if (!ARGMAX) {
         store_c(C, gr * p.ldc + gc, acc[r][c]);
       } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
