@@ -73,7 +73,7 @@ def test_colmajor_random(semi):
 
 
 @pytest.mark.parametrize("semi", SEMIS)
-@pytest.mark.parametrize("k", [1, 2, 3, 4, 31, 32, 33, 63, 64, 65, 100, 511, 1000])
+@pytest.mark.parametrize("k", [1, 2, 3, 4, 31, 32, 33, 63, 64, 65, 100, 511, 1000, 1024, 1025, 1537])
 def test_fast_path_k_tails(semi, k):
     rng = np.random.default_rng(k)
     a = rng.standard_normal((130, k)).astype(np.float32)
@@ -206,11 +206,12 @@ def test_large_square_vs_oracle_sampled_rows():
 
 @pytest.mark.parametrize("semi", SEMIS)
 @pytest.mark.parametrize("pattern", ["increasing", "decreasing", "plateau"])
-def test_argmax_improvement_patterns(semi, pattern):
+@pytest.mark.parametrize("k", [900, 1500])
+def test_argmax_improvement_patterns(semi, pattern, k):
     """Running values that improve in every k-chunk, only in the first one,
-    or tie on a long plateau: the chunk bookkeeping must give the reference's
-    first-k winner in all of them."""
-    m, k, n = 256, 1500, 256
+    or tie on a long plateau: the pair (K <= 1024) and chunk bookkeeping must
+    give the reference's first-k winner in all of them."""
+    m, n = 256, 256
     kk = np.arange(k, dtype=np.float32) * 0.01
     if semi == "minplus":
         kk = -kk
@@ -220,7 +221,7 @@ def test_argmax_improvement_patterns(semi, pattern):
         a = np.tile(-kk, (m, 1)) + 1.0
     else:
         a = np.ones((m, k), np.float32)
-        a[:, 700:900] = 2.0 if semi != "minplus" else 0.5
+        a[:, 500:800] = 2.0 if semi != "minplus" else 0.5
     a = a.astype(np.float32)
     b = np.ones((k, n), np.float32)
     c, am = engine(semi, a, b)
@@ -275,7 +276,7 @@ def test_i64_out_of_range_falls_back_exactly(semi):
 
 
 @pytest.mark.parametrize("semi", SEMIS)
-@pytest.mark.parametrize("k", [37, 300, 1001])
+@pytest.mark.parametrize("k", [37, 300, 1001, 1100])
 def test_misaligned_base_and_odd_batch_stride(semi, k):
     """A starting 4 bytes past a 16-byte boundary and odd batch strides."""
     rng = np.random.default_rng(k)
