@@ -63,6 +63,12 @@ class ClockSampler:
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait for its first sample, then
+            # keep only the samples taken from here on (the timed region)
+            t_end = time.time() + 5.0
+            while not self.lines and time.time() < t_end and self.proc.poll() is None:
+                time.sleep(0.02)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
