@@ -45,7 +45,7 @@ UNIT = "tropical_ops/s"
 
 
 class ClockSampler:
-    """nvidia-smi sampling (every 200 ms) of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi sampling (every 100 ms) of SM clock and throttle reasons during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -55,20 +55,21 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.mark = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
-            # nvidia-smi takes a moment to start: wait for its first sample, then
-            # keep only the samples taken from here on (the timed region)
+            # nvidia-smi takes a moment to start: wait for its first sample
+            # (taken under the warm-up's load), then count from here on
             t_end = time.time() + 5.0
             while not self.lines and time.time() < t_end and self.proc.poll() is None:
                 time.sleep(0.02)
-            self.lines.clear()
+            self.mark = len(self.lines)
         except OSError:
             self.proc = None
         return self
@@ -88,7 +89,11 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        # samples from the timed region; a region shorter than the sampling
+        # interval falls back to the last sample before it (under warm-up load)
+        lines = self.lines[self.mark:] or self.lines[max(0, self.mark - 1):self.mark]
+        window = "timed region" if self.lines[self.mark:] else "last warm-up sample"
+        for ln in lines:
             p = [x.strip() for x in ln.split(",")]
             if len(p) < 9:
                 continue
@@ -104,7 +109,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         loaded = [x for x in sm if x > 0.5 * (mx or max(sm))] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 def make_inputs(rows: int, seed: int = SEED):

@@ -209,6 +209,35 @@ __global__ void i32_to_f32_kernel(const int32_t* __restrict__ src, float* __rest
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
+// Stream-ordered scratch from the device's default memory pool.  A pool
+// whose release threshold is 0 (the CUDA default) hands freed memory back to
+// the OS at every synchronisation, so a caller that synchronises between
+// calls would pay a fresh mapping each time; the first allocation on a device
+// therefore raises the threshold to 1 GiB if it is still 0 (process-local:
+// the pool keeps at most that much freed memory for reuse).
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static bool tuned[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!tuned[dev]) {
+      tuned[dev] = true;
+      cudaMemPool_t pool;
+      if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t thr = 0;
+        if (cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr) == cudaSuccess && thr == 0) {
+          thr = uint64_t(1) << 30;
+          cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+        }
+      }
+      cudaGetLastError();
+    }
+  }
+  return cudaMallocAsync(p, bytes, st);
+}
+
 template <int S>
 tg_status launch_i32_via_f32(const Problem& P, cudaStream_t st) {
   // scratch rows padded to 16 bytes (the fast kernel's vector loads)
@@ -216,7 +245,7 @@ tg_status launch_i32_via_f32(const Problem& P, cudaStream_t st) {
   const int64_t asz = P.g.m * lda_f, bsz = P.g.k * ldb_f;
   const size_t bytes = size_t(P.batch) * size_t(asz + bsz) * 4 + 256;
   void* ws = nullptr;
-  cudaError_t e = cudaMallocAsync(&ws, bytes, st);
+  cudaError_t e = scratch_alloc(&ws, bytes, st);
   if (e != cudaSuccess) {  // no scratch: exact integer kernel only
     cudaGetLastError();
     return P.g.argmax ? launch_generic<S, int32_t, true>(P, st) : launch_generic<S, int32_t, false>(P, st);
@@ -283,7 +312,7 @@ tg_status launch_i64_via_f64(const Problem& P, cudaStream_t st) {
   const int64_t asz = P.g.m * lda_f, bsz = P.g.k * ldb_f;
   const size_t bytes = size_t(P.batch) * size_t(asz + bsz) * 8 + 256;
   void* ws = nullptr;
-  if (cudaMallocAsync(&ws, bytes, st) != cudaSuccess) {
+  if (scratch_alloc(&ws, bytes, st) != cudaSuccess) {
     cudaGetLastError();
     return P.g.argmax ? launch_generic<S, int64_t, true>(P, st) : launch_generic<S, int64_t, false>(P, st);
   }
