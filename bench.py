@@ -265,6 +265,63 @@ def run_case(args):
     print(json.dumps(out), flush=True)
 
 
+def sharded_extras(dist, rank, world, dev):
+    """BASELINE config 5 at this world size: M = N = 32768, K = 8192, rows of A
+    sharded across the ranks (strong scaling), B broadcast from rank 0 with
+    NCCL inside every timed step, C (+ argmax) sharded.  MaxPlus f32 with
+    argmax (A, B ~ N(0,1)) and MaxMul f64 value-only (A, B ~ U[0,1)), seed 2.
+    Every rank must call this (it runs collectives); rank 0 uses the result."""
+    from tropical_gemm import _native as Nat
+    m, n, k = 32768, 32768, 8192
+    if m % world:
+        return {"skipped": f"{m} rows do not split over {world} ranks"}
+    rows = m // world
+    lib = Nat.lib()
+    stream = torch.cuda.current_stream(dev)
+    res = {"m": m, "n": n, "k": k, "rows_per_rank": rows, "n_gpus": world,
+           "data": "torch generator seed 2 (+ rank for A) on the device"}
+    for name, dtype, semi, with_am in (("maxplus_f32_argmax", torch.float32, 0, True),
+                                       ("maxmul_f64", torch.float64, 2, False)):
+        g = torch.Generator(device=dev).manual_seed(2 + rank)
+        gb = torch.Generator(device=dev).manual_seed(2)
+        if dtype == torch.float32:
+            a = torch.randn((rows, k), generator=g, device=dev, dtype=dtype)
+            b = torch.randn((k, n), generator=gb, device=dev, dtype=dtype)
+        else:
+            a = torch.rand((rows, k), generator=g, device=dev, dtype=dtype)
+            b = torch.rand((k, n), generator=gb, device=dev, dtype=dtype)
+        c = torch.empty((rows, n), device=dev, dtype=dtype)
+        am = torch.empty((rows, n), device=dev, dtype=torch.int32) if with_am else None
+
+        def step():
+            if dist is not None:
+                dist.broadcast(b, src=0)
+            Nat.check(lib.tg_gemm(semi, Nat.DTYPES[dtype], 0, rows, n, k, a.data_ptr(), k, b.data_ptr(), n,
+                                  c.data_ptr(), n, am.data_ptr() if am is not None else None, stream.cuda_stream))
+
+        step()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = 2
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        if dist is not None:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        res[name] = {"ms_per_step": ms, "ops_per_s": float(m) * n * k / (ms * 1e-3), "steps": steps,
+                     "timing": "CUDA events per rank, max over ranks, B broadcast inside each step"}
+        del a, b, c, am
+        torch.cuda.empty_cache()
+    return res
+
+
 def dist_setup(n_gpus: int):
     if n_gpus > 1 or "RANK" in os.environ:
         import torch.distributed as dist
@@ -392,6 +449,10 @@ def run_engine(args):
             e2e_ms = float(t.item())
         e2e_value = ops_step * e2e_steps / (e2e_ms * 1e-3)
 
+    config5 = None
+    if not args.no_extras and args.size == 8192:
+        config5 = sharded_extras(dist, rank, world, dev)
+
     if rank == 0:
         peaks = measured_peaks()
         clocks = clk.summary()
@@ -431,6 +492,8 @@ def run_engine(args):
         }
         if world == 1 and not args.no_extras and args.size == 8192:
             out["extras"] = extras(dev)
+        if config5 is not None:
+            out["config5_sharded_32768x32768x8192"] = config5
         if world == 1 and not args.no_cpu:
             rows = args.cpu_rows
             threads = os.cpu_count() or 1
