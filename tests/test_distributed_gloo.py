@@ -13,7 +13,7 @@ import textwrap
 import numpy as np
 import pytest
 
-from tropical_gemm.distributed import shard_rows
+from tropical_gemm.distributed import shard_batch, shard_rows
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -35,6 +35,15 @@ def test_shard_rows_partition(m, world):
         assert a % 128 == 0
     for a, b in nonempty[:-1]:
         assert (b - a) % 128 == 0
+
+
+@pytest.mark.parametrize("batch,world", [(1, 2), (5, 2), (64, 8), (7, 3), (3, 4)])
+def test_shard_batch_partition(batch, world):
+    spans = [shard_batch(batch, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == batch
+    sizes = [b - a for a, b in spans]
+    assert all(b == c for (_, b), (c, _) in zip(spans, spans[1:]))
+    assert max(sizes) - min(sizes) <= 1
 
 
 WORKER = textwrap.dedent('''
@@ -60,6 +69,19 @@ WORKER = textwrap.dedent('''
     C = D.gather_rows(c, m); AM = D.gather_rows(am, m)
     c0, am0 = O.gemm("maxplus", a, b_full)
     assert np.array_equal(C.numpy(), c0) and np.array_equal(AM.numpy(), am0)
+    # strided-batched: shard by batch index, no exchange, gather the slices
+    bs = 5
+    ab = rng.standard_normal((bs, 20, 9)).astype(np.float32)
+    bb = rng.standard_normal((bs, 9, 11)).astype(np.float32)
+    s, e = D.shard_batch(bs, world, rank)
+    def compute_b(semi, aa, bbb, wa):
+        c, am = O.gemm_batched(semi, aa.numpy(), bbb.numpy(), wa)
+        return torch.from_numpy(c), torch.from_numpy(am)
+    cb, amb = D.sharded_batched_matmul("minplus", torch.from_numpy(ab[s:e]), torch.from_numpy(bb[s:e]),
+                                       compute=compute_b)
+    CB = D.gather_batches(cb, bs); AMB = D.gather_batches(amb, bs)
+    cb0, amb0 = O.gemm_batched("minplus", ab, bb)
+    assert np.array_equal(CB.numpy(), cb0) and np.array_equal(AMB.numpy(), amb0)
     dist.destroy_process_group()
     print("rank", rank, "ok")
 ''')

@@ -4,8 +4,9 @@ C = A (x) B where the rows of A (and of C / argmax) are split into contiguous
 blocks, one per rank, and B is needed whole by every rank.  The only exchange
 is one broadcast of B from its owner over NCCL (NVLink / NVSwitch on a B200
 node); C and argmax stay sharded, so no reduction is needed.  This is the
-multi-GPU layout the north-star names; the reference itself has no multi-GPU
-path (SURVEY: no collective call sites).
+multi-GPU layout of the engine; the reference itself has no multi-GPU path
+(its sources make no collective calls).  Strided-batched GEMMs shard by
+batch index instead and need no collective at all.
 
 One process per GPU, plumbing by torch.distributed.  Nothing here waits on a
 peer without a timeout: process groups are created with a finite timeout so a
@@ -74,3 +75,34 @@ def gather_rows(x_local: torch.Tensor, m: int, group=None) -> torch.Tensor:
     parts = [torch.empty_like(pad) for _ in range(world)]
     dist.all_gather(parts, pad, group=group)
     return torch.cat([p[: stop - start] for p, (start, stop) in zip(parts, rows)], dim=0)
+
+
+def shard_batch(batch: int, world: int, rank: int) -> Tuple[int, int]:
+    """[start, stop) of the batch indices of a strided-batched GEMM owned by
+    `rank`: contiguous, ascending in rank, sizes differing by at most one."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def sharded_batched_matmul(semiring: str, a_local: torch.Tensor, b_local: torch.Tensor, with_argmax: bool = True,
+                           compute: Optional[Callable] = None):
+    """C[p] = A[p] (x) B[p] for this rank's batch slice (as given by
+    shard_batch): every batch item is independent, so there is no exchange.
+    `compute(semiring, a, b, with_argmax)` defaults to the engine's batched GEMM."""
+    fn = compute or N.gemm_batched
+    return fn(semiring, a_local, b_local, with_argmax)
+
+
+def gather_batches(x_local: torch.Tensor, batch: int, group=None) -> torch.Tensor:
+    """All-gather batch slices (as produced by shard_batch) into the full batch."""
+    world = dist.get_world_size(group)
+    spans = [shard_batch(batch, world, r) for r in range(world)]
+    maxb = max(stop - start for start, stop in spans)
+    pad = torch.zeros((maxb,) + tuple(x_local.shape[1:]), dtype=x_local.dtype, device=x_local.device)
+    pad[: x_local.shape[0]] = x_local
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad, group=group)
+    return torch.cat([q[: stop - start] for q, (start, stop) in zip(parts, spans)], dim=0)
