@@ -29,6 +29,7 @@
 #ifndef TROPICAL_GEMM_B200_H
 #define TROPICAL_GEMM_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -87,6 +88,31 @@ tg_status tg_gemm_strided_batched(tg_semiring semiring, tg_dtype dtype, tg_layou
                                   void* c, int64_t ldc, int64_t stride_c,
                                   int32_t* argmax,
                                   void* stream);
+
+/* Broadcast callback for tg_sharded_gemm: make the `bytes` bytes of device
+ * memory at `buf` equal to rank `root`'s copy, enqueued on `stream` (for
+ * example ncclBroadcast on the caller's communicator, so the library links no
+ * collective library of its own).  Returns 0 on success. */
+typedef int (*tg_broadcast_fn)(void* buf, size_t bytes, int root, void* stream, void* ctx);
+
+/* One rank's part of a row-sharded GEMM across GPUs: B (k x n, row-major,
+ * leading dimension ldb, one buffer per rank on its device) is made whole by
+ * bcast(b, ..., root, stream, bcast_ctx), then this rank computes its own
+ * m_local rows C_local = A_local (x) B (row-major, like tg_gemm with
+ * TG_ROW_MAJOR).  C and argmax stay sharded: no reduction.  Every rank must
+ * call it (m_local may be 0: the rank still takes part in the broadcast).
+ * Column-major callers shard columns instead: pass the transposed problem
+ * (B^T rows, A^T broadcast).  No reference counterpart: the reference has no
+ * multi-GPU path; this is the sharded entry its CUDA crate would bind for one
+ * process per GPU. */
+tg_status tg_sharded_gemm(tg_semiring semiring, tg_dtype dtype,
+                          int64_t m_local, int64_t n, int64_t k,
+                          const void* a_local, int64_t lda,
+                          void* b, int64_t ldb,
+                          void* c_local, int64_t ldc,
+                          int32_t* argmax_local,
+                          int root, tg_broadcast_fn bcast, void* bcast_ctx,
+                          void* stream);
 
 /* Backward pass w.r.t. A:
  *   grad_a[i, argmax[i,j]] += grad_c[i,j] * w[i,j]

@@ -73,3 +73,37 @@ def test_python_errors_map_to_reference_types():
         N.check(N.TG_ERR_DIMENSION_MISMATCH)
     with pytest.raises(N.TropicalGemmError):
         N.check(N.TG_ERR_CUDA)
+
+
+BCAST = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p,
+                         ctypes.c_void_p)
+
+
+def _sharded_lib():
+    L = N.lib()
+    i64, vp = ctypes.c_int64, ctypes.c_void_p
+    L.tg_sharded_gemm.argtypes = [ctypes.c_int, ctypes.c_int, i64, i64, i64, vp, i64, vp, i64, vp, i64, vp,
+                                  ctypes.c_int, BCAST, vp, vp]
+    L.tg_sharded_gemm.restype = ctypes.c_int
+    return L
+
+
+def test_sharded_gemm_broadcasts_before_computing():
+    """A rank with no rows still takes part in the broadcast of B (strided
+    extent (k-1)*ldb + n elements); a failing broadcast is reported and
+    nothing is computed."""
+    L = _sharded_lib()
+    calls = []
+
+    def cb(buf, nbytes, root, stream, ctx):
+        calls.append((buf, nbytes, root))
+        return 0
+
+    f = BCAST(cb)
+    rc = L.tg_sharded_gemm(0, 1, 0, 30, 20, None, 20, 0x1000, 32, None, 30, None, 3, f, None, None)
+    assert rc == N.TG_OK and calls == [(0x1000, (19 * 32 + 30) * 8, 3)]
+    fail = BCAST(lambda *a: 7)
+    rc = L.tg_sharded_gemm(0, 0, 4, 4, 4, 0x10, 4, 0x20, 4, 0x30, 4, None, 0, fail, None, None)
+    assert rc == N.TG_ERR_CUDA and b"code 7" in L.tg_last_error()
+    rc = L.tg_sharded_gemm(0, 0, 4, 4, 4, 0x10, 4, 0x20, 4, 0x30, 4, None, 0, BCAST(0), None, None)
+    assert rc == N.TG_ERR_INVALID_ARGUMENT

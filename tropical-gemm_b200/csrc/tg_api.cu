@@ -577,6 +577,30 @@ tg_status tg_backward_b(tg_semiring semiring, tg_dtype dtype, tg_layout layout, 
                        grad_b, ldb, stride_b, accumulate, stream);
 }
 
+tg_status tg_sharded_gemm(tg_semiring semiring, tg_dtype dtype, int64_t m_local, int64_t n, int64_t k,
+                          const void* a_local, int64_t lda, void* b, int64_t ldb, void* c_local, int64_t ldc,
+                          int32_t* argmax_local, int root, tg_broadcast_fn bcast, void* bcast_ctx, void* stream) {
+  g_last_error.clear();
+  if (semiring < TG_MAXPLUS || semiring > TG_MAXMUL) return fail(TG_ERR_INVALID_ARGUMENT, "unknown semiring %d", int(semiring));
+  if (dtype < TG_F32 || dtype > TG_I64) return fail(TG_ERR_INVALID_ARGUMENT, "unknown dtype %d", int(dtype));
+  if (m_local < 0 || n < 0 || k < 0)
+    return fail(TG_ERR_INVALID_ARGUMENT, "negative size (m_local=%lld n=%lld k=%lld)", (long long)m_local, (long long)n,
+                (long long)k);
+  if (!bcast) return fail(TG_ERR_INVALID_ARGUMENT, "broadcast callback is null");
+  if (root < 0) return fail(TG_ERR_INVALID_ARGUMENT, "negative root rank %d", root);
+  // B must reach every rank even when this rank owns no rows
+  if (k > 0 && n > 0) {
+    if (!b) return fail(TG_ERR_INVALID_ARGUMENT, "B is null");
+    if (ldb < n) return fail(TG_ERR_DIMENSION_MISMATCH, "ldb=%lld < n=%lld", (long long)ldb, (long long)n);
+    const size_t elem = (dtype == TG_F64 || dtype == TG_I64) ? 8 : 4;
+    const size_t bytes = (size_t(k - 1) * size_t(ldb) + size_t(n)) * elem;
+    const int rc = bcast(b, bytes, root, stream, bcast_ctx);
+    if (rc != 0) return fail(TG_ERR_CUDA, "broadcast callback failed (code %d)", rc);
+  }
+  return tg_gemm(semiring, dtype, TG_ROW_MAJOR, m_local, n, k, a_local, lda, b, ldb, c_local, ldc, argmax_local,
+                 stream);
+}
+
 }  // extern "C"
 
 #ifdef TG_PHASE_TIMING
