@@ -149,6 +149,23 @@ def cpu_baseline(rows: int, threads: int):
     return rows * N_ * K / dt, dt
 
 
+def cpu_config1(threads: int):
+    """MaxPlus f32 + argmax, 1024^3, A and B uniform in
+    [-1, 1) from seed 0, on the reference's CPU argmax path (restated), one
+    thread and all host threads."""
+    from oracle import tg_oracle
+    rng = np.random.default_rng(0)
+    a = (2 * rng.random((1024, 1024), dtype=np.float32) - 1).astype(np.float32)
+    b = (2 * rng.random((1024, 1024), dtype=np.float32) - 1).astype(np.float32)
+    res = {}
+    for nt in (1, threads):
+        t0 = time.perf_counter()
+        tg_oracle.blis_argmax_f32("maxplus", a, b, nthreads=nt)
+        dt = time.perf_counter() - t0
+        res[f"threads_{nt}"] = {"ops_per_s": 1024.0 ** 3 / dt, "s": dt}
+    return res
+
+
 def _time_ms(fn, reps=3, warm=1):
     for _ in range(warm):
         fn()
@@ -502,6 +519,11 @@ def run_engine(args):
                                    "sample": f"{rows} x {N_} x {K} rows of the same workload, {dt:.1f} s, "
                                              "reference BLIS argmax path (mc=nc=64,kc=256, 4x4 scalar) restated "
                                              "in C, OpenMP over column blocks"}
+            # the reference runs one GEMM on one thread: the faithful figure
+            v1, dt1 = cpu_baseline(64, 1)
+            out["cpu_baseline"]["single_thread"] = {"value": v1, "cores": 1,
+                                                    "sample": f"64 x {N_} x {K} rows, {dt1:.1f} s"}
+            out["config1_cpu_1024"] = cpu_config1(threads)
         print(json.dumps(out), flush=True)
     if dist is not None:
         dist.destroy_process_group()
