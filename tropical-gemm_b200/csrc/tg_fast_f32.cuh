@@ -24,6 +24,10 @@
 //    (tropical_gemm.cu:613-618: strict update, lowest k among ties, index 0
 //    when nothing beats the semiring zero), and its exact bits (the sign of
 //    a zero included).
+//  * Short K (the host picks PAIR for K <= 1024, where the re-stream's fixed
+//    cost per output would dominate): the pair index of the last strict
+//    improvement is kept in registers and the winning k within that pair is
+//    settled in the epilogue from the two products reloaded from A and B.
 #pragma once
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
