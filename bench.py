@@ -223,7 +223,32 @@ def extras(dev):
     return res
 
 
-CASES = ("backward", "f64", "f64_values", "apsp_step", "minplus_inf")
+CASES = ("backward", "f64", "f64_values", "apsp_step", "minplus_inf", "pipe_rates")
+
+PIPE_VARIANTS = ("pair_fadd2_fmnmx3", "fadd2_alone", "fmnmx3_alone", "fadd_alone", "fmnmx_alone",
+                 "fadd_x2_fmnmx3", "fadd2_fmnmx_x2", "fadd_fmnmx")
+
+
+def pipe_rates(blocks_per_sm=(1, 2), iters=20000, variants=PIPE_VARIANTS):
+    """Register-only instruction-mix rates (products per clock per SM) from
+    the probe library (tropical-gemm_b200/csrc/probe/tg_pipe_rates.cu)."""
+    import ctypes
+    path = os.path.join(ROOT, "tropical-gemm_b200", "tropical_gemm", "libtg_pipe_rates.so")
+    lib = ctypes.CDLL(path)
+    lib.tg_probe_pipe_rate.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+    res = {}
+    for name in variants:
+        v = PIPE_VARIANTS.index(name)
+        row = {}
+        for occ in blocks_per_sm:
+            r, ms = ctypes.c_double(), ctypes.c_double()
+            rc = lib.tg_probe_pipe_rate(v, occ, 256, iters, ctypes.byref(r), ctypes.byref(ms))
+            if rc != 0:
+                raise RuntimeError(f"pipe-rate probe {name} failed with CUDA error {rc}")
+            row[f"warps_per_sm_{8 * occ}"] = round(r.value, 2)
+        res[name] = row
+    return res
 
 
 def run_case(args):
@@ -269,6 +294,8 @@ def run_case(args):
         ms = _time_ms(lambda: Nat.gemm("minplus", td, td, True), reps=args.steps, warm=args.warmup)
         out.update({"ms": ms, "ops_per_s": float(n) ** 3 / (ms * 1e-3),
                     "config": {"n": n, "dtype": "i32", "density": 0.05, "argmax": True}})
+    elif args.case == "pipe_rates":
+        out.update({"unit": "products per clock per SM", "rates": pipe_rates()})
     elif args.case == "minplus_inf":
         n = args.size
         mats = []
@@ -478,6 +505,14 @@ def run_engine(args):
         peak = props.multi_processor_count * 128 * sm_max * 1e6
         avg_kern_s = statistics.mean(kern_ms) * 1e-3
         achieved = float(M) * N_ * K / avg_kern_s
+        # second denominator: the measured rate of the kernel's own instruction
+        # mix (FADD2 + 3-input FMNMX, register-only probe, 8 warps per SM)
+        try:
+            mix = pipe_rates(blocks_per_sm=(1,), iters=4000, variants=("pair_fadd2_fmnmx3",))
+            mix = mix["pair_fadd2_fmnmx3"]["warps_per_sm_8"]
+        except Exception:  # the probe library is optional for the contract line
+            mix = None
+        mix_peak = props.multi_processor_count * mix * sm_max * 1e6 if mix else None
         out = {
             "metric": METRIC,
             "value": value,
@@ -500,7 +535,12 @@ def run_engine(args):
                          "peak_basis": f"{props.multi_processor_count} SMs x 128 ops/clk x {sm_max:.0f} MHz "
                                        "(FP32 SIMT pipes; tropical GEMM cannot use tensor cores)",
                          "frac_at_sampled_clock": (achieved / (props.multi_processor_count * 128 * clocks["sm_mhz"] * 1e6))
-                         if clocks.get("sm_mhz") else None},
+                         if clocks.get("sm_mhz") else None,
+                         "mix_peak": mix_peak / 1e12 if mix_peak else None,
+                         "frac_mix": achieved / mix_peak if mix_peak else None,
+                         "mix_basis": (f"measured FADD2 + FMNMX3 issue rate {mix:.1f} products/clk/SM "
+                                       f"(bench.py --case pipe_rates) x {props.multi_processor_count} SMs x "
+                                       f"{sm_max:.0f} MHz") if mix else None},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * (M * K + K * N_),
                     "d2h_bytes_per_step": 8 * M * N_, "api": "tropical_gemm.maxplus_matmul_dlpack"},
             "gpu_launches": args.steps,

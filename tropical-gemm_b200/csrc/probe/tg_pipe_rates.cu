@@ -1,0 +1,206 @@
+// Register-only micro-benchmark of the SIMT instruction forms a tropical
+// (max,+) GEMM can be built from on sm_100a.  It is measurement code, not part
+// of the engine: bench.py (--case pipe_rates, and every default run) loads it
+// to put a measured instruction-mix ceiling beside the pipe-count roofline.
+//
+// Every variant keeps 64 independent accumulators per thread (the engine's
+// 8x8 outputs per thread) and operands in registers, so nothing but issue,
+// operand dispatch and pipe throughput limits it.  A "product" is one
+// tropical multiply (one add) folded into an accumulator (one max); variants
+// that only add or only fold count the operation they perform.  The rate is
+// products per clock per SM, from clock64() stamps of each CTA and the SM it
+// ran on, so it does not depend on the clock frequency.
+#include <cstdint>
+#include <vector>
+#include <algorithm>
+#include <cuda_runtime.h>
+
+namespace {
+
+__device__ __forceinline__ unsigned long long pk(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fadd2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmax2(float a, float b) {
+  float r;
+  asm("max.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float fadd(float a, float b) {
+  float r;
+  asm("add.rn.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Variants (products per thread per iteration in brackets):
+//  0 pair        FADD2 + FMNMX3 per output and k-pair (the engine's loop)  [128]
+//  1 fadd2       FADD2 alone                                               [128]
+//  2 fmnmx3      FMNMX3 alone (2 folds each)                               [128]
+//  3 fadd        scalar FADD alone                                         [64]
+//  4 fmnmx       2-input FMNMX alone                                       [64]
+//  5 fadd_fmnmx3 two scalar FADD + one FMNMX3 per output and k-pair        [128]
+//  6 fadd2_fmnmx FADD2 + two 2-input FMNMX per output and k-pair           [128]
+//  7 fadd_fmnmx  scalar FADD + 2-input FMNMX per product (the reference's
+//                value-only form)                                          [64]
+template <int V>
+__global__ void __launch_bounds__(256) pipe_kernel(int iters, long long* stamps, float* sink) {
+  float acc[64];
+  const float seed = float(threadIdx.x) * 1e-3f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) acc[i] = seed + float(i) * 0.25f;
+  unsigned long long B[8];
+  float bs[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    bs[q] = -1e-3f * float(q + 1);
+    B[q] = pk(bs[q], -2e-3f * float(q + 1));
+  }
+  __syncthreads();
+  long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+    if (V == 0 || V == 5 || V == 6) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float a0 = acc[r * 8], a1 = acc[r * 8 + 1];
+        const unsigned long long A = pk(a0, a1);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float lo, hi;
+          if (V == 5) {
+            lo = fadd(a0, bs[c]);
+            hi = fadd(a1, bs[(c + 1) & 7]);
+          } else {
+            upk(fadd2(A, B[c]), lo, hi);
+          }
+          if (V == 6) acc[r * 8 + c] = fmax2(fmax2(acc[r * 8 + c], lo), hi);
+          else acc[r * 8 + c] = fmax3(acc[r * 8 + c], lo, hi);
+        }
+      }
+    } else if (V == 1) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        unsigned long long p = pk(acc[2 * i], acc[2 * i + 1]);
+        upk(fadd2(p, B[i & 7]), acc[2 * i], acc[2 * i + 1]);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        unsigned long long p = pk(acc[2 * i], acc[2 * i + 1]);
+        upk(fadd2(p, B[(i + 3) & 7]), acc[2 * i], acc[2 * i + 1]);
+      }
+    } else if (V == 2) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) acc[i] = fmax3(acc[i], bs[i & 7], bs[(i + 1) & 7]);
+    } else if (V == 3) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) acc[i] = fadd(acc[i], bs[i & 7]);
+    } else if (V == 4) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) acc[i] = fmax2(acc[i], bs[i & 7]);
+    } else if (V == 7) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float a0 = acc[r * 8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[r * 8 + c] = fmax2(acc[r * 8 + c], fadd(a0, bs[c]));
+      }
+    }
+  }
+  __syncthreads();
+  long long t1 = clock64();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) s += acc[i];
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
+  if (threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    stamps[3 * blockIdx.x] = smid;
+    stamps[3 * blockIdx.x + 1] = t0;
+    stamps[3 * blockIdx.x + 2] = t1;
+  }
+}
+
+constexpr int kProducts[8] = {128, 128, 128, 64, 64, 128, 128, 64};
+
+template <int V>
+cudaError_t launch(int blocks, int threads, int iters, long long* st, float* sink) {
+  pipe_kernel<V><<<blocks, threads>>>(iters, st, sink);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int tg_probe_variant_count(void) { return 8; }
+
+// Runs `variant` with `blocks_per_sm` CTAs of `threads` threads on every SM
+// for `iters` iterations; writes products per clock per SM (mean over SMs)
+// and the kernel's wall time in ms.  Returns 0 or a CUDA error code.
+extern "C" int tg_probe_pipe_rate(int variant, int blocks_per_sm, int threads, int iters, double* per_clk_sm,
+                                  double* ms) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = sms * blocks_per_sm;
+  long long* st = nullptr;
+  float* sink = nullptr;
+  cudaError_t e = cudaMalloc(&st, sizeof(long long) * 3 * blocks);
+  if (e == cudaSuccess) e = cudaMalloc(&sink, sizeof(float) * blocks * threads);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  if (e == cudaSuccess) {
+    using L = cudaError_t (*)(int, int, int, long long*, float*);
+    const L table[8] = {launch<0>, launch<1>, launch<2>, launch<3>, launch<4>, launch<5>, launch<6>, launch<7>};
+    const L fn = table[variant & 7];
+    e = fn(blocks, threads, 8, st, sink);   // warm-up
+    cudaEventRecord(e0);
+    if (e == cudaSuccess) e = fn(blocks, threads, iters, st, sink);
+    cudaEventRecord(e1);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+  }
+  if (e == cudaSuccess) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, e0, e1);
+    *ms = t;
+    std::vector<long long> h(3 * blocks);
+    e = cudaMemcpy(h.data(), st, sizeof(long long) * 3 * blocks, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) {
+      // per SM: products of all its CTAs over the span from the first start to the last end
+      std::vector<long long> lo(1024, -1), hi(1024, -1);
+      std::vector<int> nb(1024, 0);
+      for (int b = 0; b < blocks; ++b) {
+        const int sm = int(h[3 * b]) & 1023;
+        if (lo[sm] < 0 || h[3 * b + 1] < lo[sm]) lo[sm] = h[3 * b + 1];
+        hi[sm] = std::max(hi[sm], h[3 * b + 2]);
+        nb[sm]++;
+      }
+      double sum = 0;
+      int used = 0;
+      for (int s = 0; s < 1024; ++s)
+        if (nb[s]) {
+          sum += double(nb[s]) * threads * double(iters) * kProducts[variant & 7] / double(hi[s] - lo[s]);
+          ++used;
+        }
+      *per_clk_sm = used ? sum / used : 0.0;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(st);
+  cudaFree(sink);
+  return int(e);
+}
