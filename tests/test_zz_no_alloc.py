@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import tg_oracle
 from tropical_gemm import _native as N
 
 pytestmark = pytest.mark.gpu
@@ -52,6 +53,36 @@ def test_noalloc_matches_tg_gemm_twice(semi):
                                       c.data_ptr(), n, i.data_ptr(), st))
         torch.cuda.synchronize()
         assert torch.equal(c, c_ref) and torch.equal(i, i_ref)   # integer results: exact
+        # and the CPU oracle (the reference's GPU integer semantics, restated)
+        c_or, i_or = tg_oracle.gemm(semi, a.cpu().numpy(), b.cpu().numpy())
+        assert np.array_equal(c.cpu().numpy(), c_or) and np.array_equal(i.cpu().numpy(), i_or)
+
+
+def test_noalloc_takes_no_device_memory():
+    """Warm calls leave the device's free memory unchanged (no allocation,
+    not even a stream-ordered one), while the results stay exact."""
+    L = _lib()
+    st = torch.cuda.current_stream().cuda_stream
+    m, k, n = 512, 700, 384
+    a, b = _inputs(5, m, k, n, "minplus")
+    c = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    i = torch.empty((m, n), dtype=torch.int32, device="cuda")
+
+    def call():
+        N.check(L.tg_gemm_i32_noalloc(N.SEMIRINGS["minplus"], 0, m, n, k, a.data_ptr(), k, b.data_ptr(), n,
+                                      c.data_ptr(), n, i.data_ptr(), st))
+
+    call()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    alloc0 = torch.cuda.memory_allocated()
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0 and torch.cuda.memory_allocated() == alloc0
+    c_or, i_or = tg_oracle.gemm("minplus", a.cpu().numpy(), b.cpu().numpy())
+    assert np.array_equal(c.cpu().numpy(), c_or) and np.array_equal(i.cpu().numpy(), i_or)
 
 
 def test_noalloc_out_of_range_values_and_colmajor():

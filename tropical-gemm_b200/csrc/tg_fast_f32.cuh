@@ -35,13 +35,6 @@
 
 namespace tg {
 
-#ifdef TG_PHASE_TIMING
-__device__ long long tg_phase_ts[8192 * 6];
-#define TG_PHASE(i) do { if (threadIdx.x == 0 && blockIdx.z == 0) { unsigned bid = blockIdx.x + gridDim.x * blockIdx.y; if (bid < 8192) tg_phase_ts[bid * 6 + (i)] = clock64(); } } while (0)
-#else
-#define TG_PHASE(i) do {} while (0)
-#endif
-
 constexpr int kFBM = 128, kFBN = 128, kFBK = 32, kFThreads = 256, kFStages = 3;
 constexpr int kFApitch = kFBK + 4;                 // floats per staged A row
 constexpr int kFAStage = kFBM * kFApitch;          // floats
@@ -370,15 +363,10 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
     for (int c = 0; c < 8; ++c) {
       acc[r][c] = acc_init;
       if (ARGMAX && !PAIR) snap[r][c] = acc_init;
-#ifdef TG_PAIR_EAGER
-      if (PAIR) pidx[r][c] = 0;
-#else
       if (PAIR) pidx[r][c] = -1;
-#endif
     }
 
   // ------------------------------------------------------------ main loop
-  TG_PHASE(0);
 #pragma unroll
   for (int s = 0; s < kFStages - 1; ++s) {
     if (s < ktiles) ldr.load(s, s);
@@ -424,16 +412,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
                 Op::pair(lo, hi, a0, a1, e ? bq[q].z : bq[q].x, e ? bq[q].w : bq[q].y);
                 float& av = acc[r][2 * q + e];
                 const float nv = Op::red3(av, lo, hi);
-#ifdef TG_PAIR_EAGER
-                if (Op::better(nv, av)) {
-                  const bool first = lo == nv;
-                  pidx[r][2 * q + e] = first ? kg : kg + 1;
-                  av = first ? lo : hi;
-                }
-#else
                 if (Op::better(nv, av)) pidx[r][2 * q + e] = kg;
                 av = nv;
-#endif
               }
             } else {
               Op::pair(lo, hi, a0, a1, bq[q].x, bq[q].y);
@@ -461,7 +441,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   cp_async_wait<0>();
 
   // ------------------------------------------------------------ epilogue
-  TG_PHASE(1);
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const int lr = wm * 32 + r * 4 + lm;
@@ -475,10 +454,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
         continue;
       }
       if (PAIR) {
-#ifdef TG_PAIR_EAGER
-        store_c(C, gr * p.ldc + gc, acc[r][c]);
-        IDX[gr * p.ldc + gc] = pidx[r][c];
-#else
         // pidx: first k of the pair that held the last strict improvement
         // (-1: none, the output is (zero, 0)).  The reference's index is the
         // pair's first k whose product equals the final value; its bits are
@@ -498,7 +473,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
         }
         store_c(C, gr * p.ldc + gc, v);
         IDX[gr * p.ldc + gc] = kw;
-#endif
       } else if (!ARGMAX) {
         store_c(C, gr * p.ldc + gc, acc[r][c]);
       } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
@@ -511,7 +485,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
 
   // -------------------------------------------- argmax: bucket by chunk
   __syncthreads();
-  TG_PHASE(2);
   uint16_t* list = reinterpret_cast<uint16_t*>(sbytes + kOffList);
   uint16_t* off = reinterpret_cast<uint16_t*>(sbytes + kOffOff);
   int* cnt = reinterpret_cast<int*>(smem);            // the stages are idle after the k loop
@@ -556,7 +529,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   // index is the first k of c whose product equals that value.  Tiles of the
   // owned chunks stream through a kRStages-deep ring (the chunk ids and the
   // counters are dead now); a chunk is scanned once all its tiles have landed.
-  TG_PHASE(3);
   const RingLoader rl(A, B, p, m0, n0, tid, smem, AVEC, b_vec != 0);
   auto next_owned = [&](int c) {
     while (c < nchunks && off[c + 1] == off[c]) ++c;
@@ -726,7 +698,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
     seq0 = need;
   }
   cp_async_wait<0>();
-  TG_PHASE(4);
 }
 
 }  // namespace tg
