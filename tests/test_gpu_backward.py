@@ -188,3 +188,22 @@ def test_numpy_functions_on_gpu():
                                             torch.zeros(2, 2, dtype=torch.float64, device=dev()))
     with pytest.raises(ValueError, match="contiguous"):
         tropical_gemm.maxplus_matmul_dlpack(torch.zeros(4, 2, device=dev()).t(), torch.zeros(4, 2, device=dev()))
+
+
+@pytest.mark.parametrize("want_a", [True, False])
+def test_backward_empty_c_zeroes_every_batch(want_a):
+    """M = 0: nothing scatters, and an overwrite must zero the gradient of
+    every batch item, past the 65535 items of one grid dimension."""
+    batch, m, n, k = 65537, 0, 2, 3
+    L = N.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    if want_a:   # grad_A is M x K = 0 x 3: nothing to write, must still succeed
+        g = torch.full((batch, 1, k), float("nan"), device=dev())
+        N.check(L.tg_backward_a(0, 0, 0, batch, m, n, k, None, n, 0, None, None, n, 0, g.data_ptr(), k, k, 0, st))
+        torch.cuda.synchronize()
+        assert torch.isnan(g).all()
+    else:        # grad_B is K x N per item
+        g = torch.full((batch, k, n), float("nan"), device=dev())
+        N.check(L.tg_backward_b(0, 0, 0, batch, m, n, k, None, n, 0, None, None, k, 0, g.data_ptr(), n, k * n, 0, st))
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(g).item() == 0
