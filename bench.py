@@ -226,10 +226,13 @@ def extras(dev):
 CASES = ("backward", "f64", "f64_values", "apsp_step", "minplus_inf", "pipe_rates")
 
 PIPE_VARIANTS = ("pair_fadd2_fmnmx3", "fadd2_alone", "fmnmx3_alone", "fadd_alone", "fmnmx_alone",
-                 "fadd_x2_fmnmx3", "fadd2_fmnmx_x2", "fadd_fmnmx")
+                 "fadd_x2_fmnmx3", "fadd2_fmnmx_x2", "fadd_fmnmx", "engine_ktile_body",
+                 "engine_ktile_body_with_barrier", "ktile_body_bpair_outer", "ktile_body_two_kpairs",
+                 "ktile_body_two_kpairs_tree", "ktile_body_kquad_swapped", "ktile_body_kquad_aligned")
 
 
 def pipe_rates(blocks_per_sm=(1, 2), iters=20000, variants=PIPE_VARIANTS):
+    # the k-tile body variants run one CTA per SM (their register use)
     """Register-only instruction-mix rates (products per clock per SM) from
     the probe library (tropical-gemm_b200/csrc/probe/tg_pipe_rates.cu)."""
     import ctypes
@@ -241,9 +244,10 @@ def pipe_rates(blocks_per_sm=(1, 2), iters=20000, variants=PIPE_VARIANTS):
     for name in variants:
         v = PIPE_VARIANTS.index(name)
         row = {}
-        for occ in blocks_per_sm:
+        for occ in (blocks_per_sm if v < 8 else (1,)):
+            it = iters if v < 8 else max(1, iters // 32)
             r, ms = ctypes.c_double(), ctypes.c_double()
-            rc = lib.tg_probe_pipe_rate(v, occ, 256, iters, ctypes.byref(r), ctypes.byref(ms))
+            rc = lib.tg_probe_pipe_rate(v, occ, 256, it, ctypes.byref(r), ctypes.byref(ms))
             if rc != 0:
                 raise RuntimeError(f"pipe-rate probe {name} failed with CUDA error {rc}")
             row[f"warps_per_sm_{8 * occ}"] = round(r.value, 2)

@@ -14,6 +14,7 @@
 #include <vector>
 #include <algorithm>
 #include <cuda_runtime.h>
+#include "../tg_fast_f32.cuh"
 
 namespace {
 
@@ -56,6 +57,7 @@ __device__ __forceinline__ float fadd(float a, float b) {
 //  6 fadd2_fmnmx FADD2 + two 2-input FMNMX per output and k-pair           [128]
 //  7 fadd_fmnmx  scalar FADD + 2-input FMNMX per product (the reference's
 //                value-only form)                                          [64]
+//  8, 9          the engine's k-tile body from shared memory (below)
 template <int V>
 __global__ void __launch_bounds__(256) pipe_kernel(int iters, long long* stamps, float* sink) {
   float acc[64];
@@ -134,17 +136,179 @@ __global__ void __launch_bounds__(256) pipe_kernel(int iters, long long* stamps,
   }
 }
 
-constexpr int kProducts[8] = {128, 128, 128, 64, 64, 128, 128, 64};
+// Variants 8 and 9: the engine's own k-tile body (tg::tile_math, MaxPlus,
+// values only) over one shared-memory stage that never changes; 9 adds the
+// k loop's barrier per k-tile.  Products per iteration: 64 outputs x 32 k.
+template <int V>
+__global__ void __launch_bounds__(256, 1) body_kernel(int iters, long long* stamps, float* sink) {
+  extern __shared__ __align__(16) float stage[];
+  for (int i = threadIdx.x; i < tg::kFStageFloats; i += blockDim.x) stage[i] = float((i * 37) % 101) * 0.01f;
+  __syncthreads();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float acc[8][8];
+  int32_t unused[1][1];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[r][c] = -1e30f;
+  long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+    if (V == 9) __syncthreads();
+    tg::tile_math<tg::kMaxPlus, false>(stage, warp >> 1, warp & 1, lane >> 3, lane & 7, acc, unused, 0);
+  }
+  __syncthreads();
+  long long t1 = clock64();
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) s += acc[r][c];
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
+  if (threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    stamps[3 * blockIdx.x] = smid;
+    stamps[3 * blockIdx.x + 1] = t0;
+    stamps[3 * blockIdx.x + 2] = t1;
+  }
+}
+
+// Variants 10-12: alternative orders of the same k-tile body (each with the
+// barrier per k-tile), to see which operand order the SIMT pipes prefer.
+//  10: B pair outer (each B k-pair register pair feeds eight FADD2 in a row)
+//  11: two k-pairs per output back to back (two independent FADD2, then two FMNMX3)
+//  12: two k-pairs folded by a 3-input max tree (t = max(lo0, hi0, lo1); acc = max(acc, t, hi1))
+//  13: B staged as one float4 of four k per column with its two k-pairs swapped,
+//      so each FADD2 pairs A's (x,y) with B's (z,w) registers and vice versa
+//  14: as 13 without the swap (A's (x,y) with B's (x,y))
+__device__ __forceinline__ void fadd2s(float& lo, float& hi, float a0, float a1, float b0, float b1) {
+  tg::FastOps<tg::kMaxPlus>::pair(lo, hi, a0, a1, b0, b1);
+}
+__device__ __forceinline__ float mx3(float a, float b, float c) { return tg::FastOps<tg::kMaxPlus>::red3(a, b, c); }
+
+template <int V>
+__device__ __forceinline__ void alt_body(const float* stage, int wm, int wn, int lm, int ln, float (&acc)[8][8]) {
+  const float* Ap = stage + (wm * 32 + lm) * tg::kFApitch;
+  const float* Bp = stage + tg::kFAStage + (wn * 64 + 2 * ln) * 2;
+#pragma unroll
+  for (int k4 = 0; k4 < tg::kFBK; k4 += 4) {
+    float4 a[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) a[r] = *reinterpret_cast<const float4*>(Ap + r * 4 * tg::kFApitch + k4);
+    if (V == 13 || V == 14) {
+      // one float4 of B per column holding four k (k-pair order swapped for 13),
+      // the thread's columns wn*64 + ln + 8c
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 b = *reinterpret_cast<const float4*>(stage + tg::kFAStage + ((k4 / 4) * tg::kFBN + wn * 64 + ln + 8 * c) * 4);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          float l0, h0, l1, h1;
+          if (V == 13) {
+            fadd2s(l0, h0, a[r].x, a[r].y, b.z, b.w);
+            fadd2s(l1, h1, a[r].z, a[r].w, b.x, b.y);
+          } else {
+            fadd2s(l0, h0, a[r].x, a[r].y, b.x, b.y);
+            fadd2s(l1, h1, a[r].z, a[r].w, b.z, b.w);
+          }
+          acc[r][c] = mx3(mx3(acc[r][c], l0, h0), l1, h1);
+        }
+      }
+    } else if (V == 10) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float4 bq[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bq[q] = *reinterpret_cast<const float4*>(Bp + (k4 / 2 + h) * (tg::kFBN * 2) + q * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              float lo, hi;
+              fadd2s(lo, hi, h ? a[r].z : a[r].x, h ? a[r].w : a[r].y, e ? bq[q].z : bq[q].x, e ? bq[q].w : bq[q].y);
+              acc[r][2 * q + e] = mx3(acc[r][2 * q + e], lo, hi);
+            }
+      }
+    } else {
+      float4 b0[4], b1[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        b0[q] = *reinterpret_cast<const float4*>(Bp + (k4 / 2) * (tg::kFBN * 2) + q * 32);
+        b1[q] = *reinterpret_cast<const float4*>(Bp + (k4 / 2 + 1) * (tg::kFBN * 2) + q * 32);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float l0, h0, l1, h1;
+            fadd2s(l0, h0, a[r].x, a[r].y, e ? b0[q].z : b0[q].x, e ? b0[q].w : b0[q].y);
+            fadd2s(l1, h1, a[r].z, a[r].w, e ? b1[q].z : b1[q].x, e ? b1[q].w : b1[q].y);
+            if (V == 11) {
+              acc[r][2 * q + e] = mx3(mx3(acc[r][2 * q + e], l0, h0), l1, h1);
+            } else {
+              acc[r][2 * q + e] = mx3(acc[r][2 * q + e], mx3(l0, h0, l1), h1);
+            }
+          }
+    }
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(256, 1) alt_kernel(int iters, long long* stamps, float* sink) {
+  extern __shared__ __align__(16) float stage[];
+  for (int i = threadIdx.x; i < tg::kFStageFloats; i += blockDim.x) stage[i] = float((i * 37) % 101) * 0.01f;
+  __syncthreads();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float acc[8][8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[r][c] = -1e30f;
+  long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+    __syncthreads();
+    alt_body<V>(stage, warp >> 1, warp & 1, lane >> 3, lane & 7, acc);
+  }
+  __syncthreads();
+  long long t1 = clock64();
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) s += acc[r][c];
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
+  if (threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    stamps[3 * blockIdx.x] = smid;
+    stamps[3 * blockIdx.x + 1] = t0;
+    stamps[3 * blockIdx.x + 2] = t1;
+  }
+}
+
+constexpr int kVariants = 15;
+constexpr int kProducts[kVariants] = {128, 128, 128, 64, 64, 128, 128, 64, 64 * tg::kFBK, 64 * tg::kFBK,
+                                      64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK};
 
 template <int V>
 cudaError_t launch(int blocks, int threads, int iters, long long* st, float* sink) {
-  pipe_kernel<V><<<blocks, threads>>>(iters, st, sink);
+  if constexpr (V >= 10) {
+    alt_kernel<V><<<blocks, threads, tg::kFStageFloats * 4>>>(iters, st, sink);
+  } else if constexpr (V >= 8) {
+    body_kernel<V><<<blocks, threads, tg::kFStageFloats * 4>>>(iters, st, sink);
+  } else {
+    pipe_kernel<V><<<blocks, threads>>>(iters, st, sink);
+  }
   return cudaGetLastError();
 }
 
 }  // namespace
 
-extern "C" int tg_probe_variant_count(void) { return 8; }
+extern "C" int tg_probe_variant_count(void) { return kVariants; }
 
 // Runs `variant` with `blocks_per_sm` CTAs of `threads` threads on every SM
 // for `iters` iterations; writes products per clock per SM (mean over SMs)
@@ -164,8 +328,11 @@ extern "C" int tg_probe_pipe_rate(int variant, int blocks_per_sm, int threads, i
   cudaEventCreate(&e1);
   if (e == cudaSuccess) {
     using L = cudaError_t (*)(int, int, int, long long*, float*);
-    const L table[8] = {launch<0>, launch<1>, launch<2>, launch<3>, launch<4>, launch<5>, launch<6>, launch<7>};
-    const L fn = table[variant & 7];
+    const L table[kVariants] = {launch<0>, launch<1>, launch<2>, launch<3>, launch<4>,
+                                launch<5>, launch<6>, launch<7>, launch<8>, launch<9>,
+                                launch<10>, launch<11>, launch<12>, launch<13>, launch<14>};
+    if (variant < 0 || variant >= kVariants) variant = 0;
+    const L fn = table[variant];
     e = fn(blocks, threads, 8, st, sink);   // warm-up
     cudaEventRecord(e0);
     if (e == cudaSuccess) e = fn(blocks, threads, iters, st, sink);
@@ -192,7 +359,7 @@ extern "C" int tg_probe_pipe_rate(int variant, int blocks_per_sm, int threads, i
       int used = 0;
       for (int s = 0; s < 1024; ++s)
         if (nb[s]) {
-          sum += double(nb[s]) * threads * double(iters) * kProducts[variant & 7] / double(hi[s] - lo[s]);
+          sum += double(nb[s]) * threads * double(iters) * kProducts[variant] / double(hi[s] - lo[s]);
           ++used;
         }
       *per_clk_sm = used ? sum / used : 0.0;

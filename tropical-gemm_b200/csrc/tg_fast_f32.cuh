@@ -191,6 +191,19 @@ struct BLoader {
 
   __device__ __forceinline__ void load(uint32_t soff, int64_t kt) const {
     const int64_t k0 = kt * kFBK;
+#ifdef TG_EXP_B16
+    {  // experiment: the cost of four 16-byte copies per thread (wrong layout)
+      const float* b0 = src - kpar * (step >> 1);
+      const uint32_t d0 = dst - uint32_t(((threadIdx.x & 127) * 2 + kpar) * 4);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int lin = threadIdx.x + e * kFThreads;
+        const int kk = lin >> 5, c = (lin & 31) * 4;
+        cp_async16(d0 + soff + uint32_t((kk * kFBN + c) * 4), b0 + (k0 + kk) * (step >> 1) + c - (threadIdx.x & 127), 16);
+      }
+      return;
+    }
+#endif
     const float* s = src + k0 * (step >> 1);
     if (k0 + kFBK <= k) {
       const int bytes = colok ? 4 : 0;

@@ -219,6 +219,9 @@ fast_f32_argmax_kernel(GemmArgs p, int64_t nbatch, int tpc, int b_vec, float acc
 
   float acc[8][8], snap[8][8];
   int32_t pidx_unused[1][1];
+#ifdef TG_EXP_CLK
+  long long dbg[4] = {0, 0, 0, 0};
+#endif
   while (have) {
     const bool has_cur = cur >= 0, has_prv = prv >= 0;
     const TileAt cc = tile_at(has_cur ? cur : 0, tiles_m, tiles_n);
@@ -243,8 +246,15 @@ fast_f32_argmax_kernel(GemmArgs p, int64_t nbatch, int tpc, int b_vec, float acc
     int32_t rs_k = 0;
 
     for (int64_t t = 0; t < ktiles; ++t) {
+#ifdef TG_EXP_CLK
+      long long c0 = clock64();
+#endif
       cp_async_wait<kFStages - 2>();
       __syncthreads();
+#ifdef TG_EXP_CLK
+      long long c1 = clock64();
+      if (has_cur && has_prv) dbg[0] += c1 - c0;
+#endif
       float* stage = smem + (t % kFStages) * kPStageFloats;
       if (t == ktiles - 1 && kvalid_last < kFBK) {
         fix_k_tail<S>(stage, kvalid_last, tid);
@@ -306,7 +316,16 @@ fast_f32_argmax_kernel(GemmArgs p, int64_t nbatch, int tpc, int b_vec, float acc
         }
       }
 
+#ifdef TG_EXP_CLK
+      long long c2 = clock64();
+      if (has_cur && has_prv) dbg[1] += c2 - c1;
+#endif
       if (has_cur) tile_math<S, false>(stage, wm, wn, lm, ln, acc, pidx_unused, 0);
+#ifdef TG_EXP_CLK
+      long long c3 = clock64();
+      if (has_cur && has_prv) dbg[2] += c3 - c2;
+      if (!has_cur) dbg[3] += c3 - c0;
+#endif
 
       if (has_cur && ((t + 1) % tpc == 0 || t == ktiles - 1)) {
         // chunk boundary: remember the chunk of each output's latest strict improvement
@@ -388,6 +407,11 @@ fast_f32_argmax_kernel(GemmArgs p, int64_t nbatch, int tpc, int b_vec, float acc
     __syncthreads();
   }
   cp_async_wait<0>();
+#ifdef TG_EXP_CLK
+  // experiment only: per-warp cycle sums (wait+barrier, scan, math, drain) into argmax[]
+  if (lane == 0)
+    for (int i = 0; i < 4; ++i) p.argmax[(int64_t(blockIdx.x) * 8 + warp) * 4 + i] = int32_t(dbg[i] >> 8);
+#endif
 }
 
 }  // namespace tg
