@@ -20,7 +20,14 @@
  *    plain kernels (tropical_gemm.cu:1043-1050): NaN operands are ignored and
  *    max(+0,-0) = +0, min(+0,-0) = -0 (behaviour measured on sm_100).
  *
- * Build: see oracle/Makefile (gcc -O2 -fopenmp -ffp-contract=off, no fast-math).
+ *  - the reference CPU SIMD path without argmax for MaxPlus f32
+ *    (crates/tropical-gemm/src/simd/dispatch.rs:44-84 picking
+ *    Avx2MaxPlusF32Kernel, simd/kernels/avx2.rs:12-74, with
+ *    TilingParams::F32_AVX2 mc=nc=256, kc=512, mr=nr=8; core/tiling.rs:21-27;
+ *    5-loop driver core/gemm.rs:56-140).
+ *
+ * Build: see oracle/Makefile (gcc -O3 -mavx2 -mfma -fopenmp -ffp-contract=off,
+ * no fast-math).
  */
 #include <math.h>
 #include <stdint.h>
@@ -28,6 +35,9 @@
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
+#endif
+#if defined(__AVX2__)
+#include <immintrin.h>
 #endif
 
 enum { MAXPLUS = 0, MINPLUS = 1, MAXMUL = 2 };
@@ -191,6 +201,88 @@ int tg_oracle_blis_argmax_f32(int semiring, int64_t m, int64_t n, int64_t k, con
     free(pb);
   }
   return 0;
+}
+
+/*
+ * The reference CPU SIMD value-only path for MaxPlus f32: BLIS 5-loop
+ * blocking (jc over nc=256, pc over kc=512, ic over mc=256), A packed into
+ * 8-row slivers and B into 8-column slivers, and an 8x8 microkernel that
+ * keeps one 8-lane vector per row of C: acc[i] = max(acc[i], a[i] + b[0..8)).
+ * The vector max is the AVX `max_ps(acc, product)` that the reference's
+ * f32x8::max compiles to, so NaN behaviour follows that instruction (not
+ * pinned by any reference test).  C is read and written per kc block, as in
+ * the reference, starting from the semiring zero.  nthreads > 1 splits the
+ * jc loop (per-thread packing buffers; identical arithmetic per output).
+ * Returns 1 when the build has no AVX2.
+ */
+#define SMC 256
+#define SNC 256
+#define SKC 512
+#define SMR 8
+#define SNR 8
+
+int tg_oracle_simd_maxplus_f32(int64_t m, int64_t n, int64_t k, const float* a, const float* b, float* c,
+                               int nthreads) {
+#if defined(__AVX2__)
+  if (nthreads < 1) nthreads = 1;
+  for (int64_t e = 0; e < m * n; ++e) c[e] = -INFINITY;
+  if (m == 0 || n == 0 || k == 0) return 0;
+  const int64_t njc = (n + SNC - 1) / SNC;
+  _Pragma("omp parallel num_threads(nthreads)")
+  {
+    float* pa = (float*)aligned_alloc(32, sizeof(float) * SMC * SKC);
+    float* pb = (float*)aligned_alloc(32, sizeof(float) * SKC * SNC);
+    _Pragma("omp for schedule(dynamic, 1)")
+    for (int64_t jb = 0; jb < njc; ++jb) {
+      const int64_t jc = jb * SNC, nc = (n - jc) < SNC ? (n - jc) : SNC;
+      for (int64_t pc = 0; pc < k; pc += SKC) {
+        const int64_t kc = (k - pc) < SKC ? (k - pc) : SKC;
+        for (int64_t jr = 0; jr < nc; jr += SNR)
+          for (int64_t p = 0; p < kc; ++p)
+            for (int j = 0; j < SNR; ++j)
+              pb[jr * kc + p * SNR + j] = (jr + j < nc) ? b[(pc + p) * n + jc + jr + j] : 0.0f;
+        for (int64_t ic = 0; ic < m; ic += SMC) {
+          const int64_t mc = (m - ic) < SMC ? (m - ic) : SMC;
+          for (int64_t ir = 0; ir < mc; ir += SMR)
+            for (int64_t p = 0; p < kc; ++p)
+              for (int i = 0; i < SMR; ++i)
+                pa[ir * kc + p * SMR + i] = (ir + i < mc) ? a[(ic + ir + i) * k + pc + p] : 0.0f;
+          for (int64_t jr = 0; jr < nc; jr += SNR) {
+            const int nr = (nc - jr) < SNR ? (int)(nc - jr) : SNR;
+            for (int64_t ir = 0; ir < mc; ir += SMR) {
+              const int mr = (mc - ir) < SMR ? (int)(mc - ir) : SMR;
+              float* cp = c + (ic + ir) * n + jc + jr;
+              const float* ap = pa + ir * kc;
+              const float* bp = pb + jr * kc;
+              __m256 acc[SMR];
+              for (int i = 0; i < SMR; ++i) {
+                float row[SNR];
+                for (int j = 0; j < SNR; ++j) row[j] = (i < mr && j < nr) ? cp[i * n + j] : -INFINITY;
+                acc[i] = _mm256_loadu_ps(row);
+              }
+              for (int64_t p = 0; p < kc; ++p) {
+                const __m256 bv = _mm256_loadu_ps(bp + p * SNR);
+                for (int i = 0; i < SMR; ++i)
+                  acc[i] = _mm256_max_ps(acc[i], _mm256_add_ps(_mm256_set1_ps(ap[p * SMR + i]), bv));
+              }
+              for (int i = 0; i < mr; ++i) {
+                float row[SNR];
+                _mm256_storeu_ps(row, acc[i]);
+                for (int j = 0; j < nr; ++j) cp[i * n + j] = row[j];
+              }
+            }
+          }
+        }
+      }
+    }
+    free(pa);
+    free(pb);
+  }
+  return 0;
+#else
+  (void)m; (void)n; (void)k; (void)a; (void)b; (void)c; (void)nthreads;
+  return 1;
+#endif
 }
 
 /*

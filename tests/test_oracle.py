@@ -37,6 +37,25 @@ def test_blis_path_matches_fixtures(name):
     assert np.array_equal(c, FIX[name + "__c"]) and np.array_equal(am, FIX[name + "__argmax"])
 
 
+@pytest.mark.parametrize("name", [n for n in NAMES if n.startswith("maxplus_f32") and "batched" not in n])
+def test_simd_value_path_matches_fixtures(name):
+    """The restated reference CPU SIMD path (AVX2 8x8 microkernel, no argmax)."""
+    a, b = FIX[name + "__a"], FIX[name + "__b"]
+    c = O.simd_maxplus_f32(a, b, nthreads=2)
+    assert np.array_equal(c.view(np.uint32), FIX[name + "__c"].view(np.uint32))
+
+
+def test_simd_value_path_matches_argmax_path_across_blocks():
+    """Shapes past every block size (mc = nc = 256, kc = 512) and ragged edges:
+    the SIMD values equal the argmax path's (finite inputs)."""
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((300, 1100), dtype=np.float32)
+    b = rng.standard_normal((1100, 270), dtype=np.float32)
+    c_simd = O.simd_maxplus_f32(a, b, nthreads=3)
+    c_ref, _ = O.blis_argmax_f32("maxplus", a, b, nthreads=3)
+    assert np.array_equal(c_simd, c_ref)
+
+
 def test_known_answer_2x3_3x2():
     """crates/tropical-gemm-cuda/src/lib.rs:1091-1191 (column-major data there, row-major here)."""
     a = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
