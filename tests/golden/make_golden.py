@@ -22,7 +22,9 @@ SCALARS = {"f32": np.float32, "f64": np.float64}
 
 
 def main() -> None:
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (or set REF_ROOT)")
     fdir = os.path.join(root, "crates/tropical-gemm-python/tests/fixtures")
     out = {}
     names = []
