@@ -49,8 +49,12 @@ tg_status check_launch(const char* what) {
 }
 
 bool fast_f32_ok(const Problem& P) {
-  // any A alignment (4-byte copies for unaligned rows); chunk length grows with K
-  return P.g.k < (int64_t(1) << 31);
+  const auto& g = P.g;
+  // any A alignment: the kernel switches to 4-byte copies for unaligned rows
+  if (g.k >= (int64_t(1) << 31)) return false;
+  // argmax: the re-stream ring holds whole chunks of <= 4 k-tiles (1024 chunks)
+  if (g.argmax && (g.k + tg::kFBK - 1) / tg::kFBK > int64_t(4) * tg::kFMaxChunks) return false;
+  return true;
 }
 
 // Per-device launch configuration, set up once per (device, kernel) under a

@@ -29,42 +29,40 @@ __global__ void fill_zero_kernel(T* c, int32_t* idx, int64_t m, int64_t n, int64
   }
 }
 
-// Argmax by k-pair tracking up to this K (the tracking costs ~2 instructions
-// per product, a price per output that the chunk path beats beyond it).
 constexpr int64_t kPairMaxK = 1024;
 
 template <int S, bool ARGMAX, bool OUTI = false>
 tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
+  const size_t smem = ARGMAX ? tg::kFSmemArgmax : tg::kFSmemValues;
+  // variant: argmax by chunk re-stream or by k-pair tracking (short K);
   // A staged by 16-byte copies when every batch's A rows are 16-byte aligned
-  // (the i32 path stages padded, aligned copies)
-  const bool avec = OUTI || ((reinterpret_cast<uintptr_t>(P.g.a) & 15) == 0 && P.g.lda % 4 == 0 &&
-                             (P.batch == 1 || P.g.sa % 4 == 0));
+  const bool pair = ARGMAX && P.g.k <= kPairMaxK;
+  const bool avec = (reinterpret_cast<uintptr_t>(P.g.a) & 15) == 0 && P.g.lda % 4 == 0 &&
+                    (P.batch == 1 || P.g.sa % 4 == 0);
+  using KernT = void (*)(tg::GemmArgs, int, int, float);
+  KernT kern;
+  int variant;
+  if constexpr (OUTI) {   // the i32 path stages padded, aligned copies
+    kern = pair ? tg::fast_f32_kernel<S, ARGMAX, OUTI, true> : tg::fast_f32_kernel<S, ARGMAX, OUTI, false>;
+    variant = pair ? 1 : 0;
+  } else {
+    if (pair) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true> : tg::fast_f32_kernel<S, ARGMAX, false, true, false>;
+    else kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, false, true> : tg::fast_f32_kernel<S, ARGMAX, false, false, false>;
+    variant = (pair ? 1 : 0) + (avec ? 0 : 2);
+  }
+  {
+    tg_status s = ensure_smem(reinterpret_cast<const void*>(kern), smem);
+    if (s != TG_OK) return s;
+  }
+  const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
+  int tpc = 2;
+  const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
+                     (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
+  while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
+  // (Short K: the re-stream costs as much per output as at long K, so the
+  // argmax is tracked per k-pair in registers instead; measured crossover K ~ 1024-1536.)
   const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;
   const int64_t gy = (P.g.n + tg::kFBN - 1) / tg::kFBN;
-  if (ARGMAX && P.g.k > kPairMaxK) {
-    // persistent chunk-detection kernel, one CTA per SM
-    using KernT = void (*)(tg::GemmArgs, int64_t, int, int, float);
-    KernT kern;
-    if constexpr (OUTI) kern = tg::fast_f32_argmax_kernel<S, true, true>;
-    else kern = avec ? tg::fast_f32_argmax_kernel<S, false, true> : tg::fast_f32_argmax_kernel<S, false, false>;
-    tg_status s = ensure_smem(reinterpret_cast<const void*>(kern), tg::kFSmemArgmax);
-    if (s != TG_OK) return s;
-    const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
-    int tpc = 2;
-    while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
-    const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
-                       (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
-    const int64_t tiles = P.batch * gx * gy;
-    const int64_t grid = std::min<int64_t>(tiles, sm_count());
-    kern<<<unsigned(grid), tg::kFThreads, tg::kFSmemArgmax, st>>>(P.g, P.batch, tpc, b_vec, acc_init);
-    return check_launch("fast_f32_argmax_kernel launch");
-  }
-  using KernT = void (*)(tg::GemmArgs, float);
-  KernT kern;
-  if constexpr (OUTI) kern = tg::fast_f32_kernel<S, ARGMAX, true, true>;
-  else kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true> : tg::fast_f32_kernel<S, ARGMAX, false, false>;
-  tg_status s = ensure_smem(reinterpret_cast<const void*>(kern), tg::kFSmemValues);
-  if (s != TG_OK) return s;
   if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
   for (int64_t b0 = 0; b0 < P.batch; b0 += 65535) {
     const int64_t nb = std::min<int64_t>(65535, P.batch - b0);
@@ -73,8 +71,8 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
     g.b = static_cast<const float*>(g.b) + b0 * g.sb;
     g.c = static_cast<float*>(g.c) + b0 * g.sc;
     if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
-    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, tg::kFSmemValues, st>>>(g, acc_init);
-    s = check_launch("fast_f32_kernel launch");
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec, acc_init);
+    tg_status s = check_launch("fast_f32_kernel launch");
     if (s != TG_OK) return s;
   }
   return TG_OK;

@@ -1,5 +1,5 @@
 // B200 fast path for f32 tropical GEMM (all three semirings, with or
-// without argmax).
+// without argmax), one launch for a whole strided batch.
 //
 // Why it looks like this (sm_100a, no tensor cores for (max,+)):
 //  * Two products per instruction on each SIMT pipe: products come from
@@ -13,15 +13,21 @@
 //    ([k/2][n][2]) by 4-byte cp.async, so its k-pair is a register pair too.
 //  * 128x128x32 CTA tiles, 256 threads, 8x8 outputs per thread, 3-stage
 //    cp.async pipeline, one CTA per SM (register bound).
-//
-// Kernels:
-//  * fast_f32_kernel<S, ARGMAX = false>: values only, one CTA per tile.
-//  * fast_f32_kernel<S, ARGMAX = true> (short K; the host picks it for
-//    K <= 1024): the pair index of the last strict improvement is kept in
-//    registers and the winning k within that pair is settled in the
-//    epilogue from the two products reloaded from A and B.
-//  * fast_f32_argmax_kernel (tg_fast_f32_argmax.cuh): long K, persistent,
-//    argmax by chunk detection resolved inside the next tile's k loop.
+//  * Argmax without a per-product compare: the value accumulator runs
+//    free over a chunk of L k's; at each chunk boundary one strict compare
+//    against the snapshot taken at the previous boundary records the chunk
+//    of the last strict improvement (the chunk holding the first k that
+//    attains the final value).  After the k loop the CTA buckets its outputs
+//    by that chunk, re-streams only the chunks that own outputs, and scans
+//    each owned chunk from shared memory for the first k whose product
+//    equals the final value -- exactly the reference's winner
+//    (tropical_gemm.cu:613-618: strict update, lowest k among ties, index 0
+//    when nothing beats the semiring zero), and its exact bits (the sign of
+//    a zero included).
+//  * Short K (the host picks PAIR for K <= 1024, where the re-stream's fixed
+//    cost per output would dominate): the pair index of the last strict
+//    improvement is kept in registers and the winning k within that pair is
+//    settled in the epilogue from the two products reloaded from A and B.
 #pragma once
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
@@ -34,11 +40,35 @@ constexpr int kFApitch = kFBK + 4;                 // floats per staged A row
 constexpr int kFAStage = kFBM * kFApitch;          // floats
 constexpr int kFBStage = kFBK * kFBN;              // floats
 constexpr int kFStageFloats = kFAStage + kFBStage;
+constexpr int kFMaxChunks = 1024;
+constexpr uint16_t kNoChunk = 0xFFFF;              // output never beat the semiring zero
 constexpr size_t kFSmemValues = size_t(kFStages) * kFStageFloats * 4;
-#ifndef TG_K4_UNROLL
-#define TG_K4_UNROLL 8
-#endif
-constexpr int kK4Unroll = TG_K4_UNROLL;   // unrolled 4-k steps of the k-tile loop body
+// Argmax kernel shared-memory map.  During the k loop: the three pipeline
+// stages and one chunk id (u16) per CTA output.  After the outputs are
+// bucketed by chunk, kRStages ring slots (overlaying stages and chunk ids)
+// re-stream the owned chunks -- three two-tile chunks resident or in flight,
+// so the scan of one chunk overlaps the copies of the next two; the bucketed
+// list and its u16 offsets sit above the ring.
+constexpr int kRStages = 6;
+constexpr int kRAFloats = kFBM * kFBK;                     // A slot: 128 rows x 32 k, 16-byte groups swizzled
+constexpr int kRStageFloats = kRAFloats + kFBK * kFBN;     // + B slot: 32 k x 128 n, swizzled
+constexpr size_t kOffCid = kFSmemValues;
+constexpr size_t kOffList = size_t(kRStages) * kRStageFloats * 4;
+constexpr size_t kOffOff = kOffList + size_t(kFBM * kFBN) * 2;
+constexpr size_t kFSmemArgmax = kOffOff + size_t(kFMaxChunks + 1) * 2;
+static_assert(kOffCid + size_t(kFBM * kFBN) * 2 <= kOffList, "chunk ids overlap the list");
+static_assert(size_t(2 * (kFMaxChunks + 1)) * 4 <= kOffCid, "bucket counters overlap the chunk ids");
+static_assert(kFSmemArgmax <= 232448, "argmax kernel exceeds shared memory");
+static_assert(kFBM * kFBN <= 65535, "u16 bucket offsets");
+
+// Ring-slot element positions.  Rows keep their natural length (no padding);
+// instead the 16-byte groups of a row are XOR-swizzled by the row index, so
+// the scan's column reads (4 lanes on consecutive k of one output, 8 outputs
+// per warp) spread over the banks.
+__device__ __forceinline__ int ring_a(int r, int k) { return r * kFBK + ((((k >> 2) ^ (r & 7)) << 2) | (k & 3)); }
+__device__ __forceinline__ int ring_b(int k, int n) {
+  return kRAFloats + k * kFBN + ((((n >> 2) ^ (k & 7)) << 2) | (n & 3));
+}
 
 template <int S> struct FastOps;
 template <> struct FastOps<kMaxPlus> {
@@ -99,125 +129,169 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" :: "n"(N));
 }
 
-// Per-thread staging of the A side of one k-tile (128 rows x 32 k, row-major,
-// kFApitch floats per row), every address term that does not depend on the
-// k-tile precomputed.  Thread t copies rows (t>>3) + 32e, e = 0..3, at k
-// offset 4*(t&7) as 16-byte cp.async; unaligned A rows (lda % 4 != 0 or a
-// misaligned base) use 4-byte copies instead.  Out-of-range rows and k are
-// zero-filled (src-size 0); the k tail of the last tile is fixed up by
-// fix_k_tail.
-struct ALoader {
-  const float* src;     // A + (m0 + (t>>3)) * lda + 4*(t&7)
-  const float* base;    // A + m0 * lda
-  int64_t step;         // 32 * lda
-  int64_t k, lda, rows;
-  uint32_t dst;         // this thread's stage-0 destination
-  uint32_t smem;        // stage-0 A base
-  int kq, tid;
-  uint32_t rowmask;     // bit e: row (t>>3) + 32e exists
-  bool vec;
+// Per-thread staging of k-tiles into one pipeline stage, with every address
+// term that does not depend on the tile precomputed once per CTA.
+//  A: 128 rows x 32 k as 16-byte cp.async; thread t copies rows
+//     (t>>3) + 32e, e = 0..3, at k offset 4*(t&7).
+//  B: 32 k x 128 n as 4-byte cp.async into the k-pair-interleaved layout;
+//     thread t copies column t&127 for rows (t>>7) + 2e, e = 0..15, so its
+//     shared-memory destinations are 1 KiB apart and its sources 2*ldb apart.
+// Out-of-range rows/columns are zero-filled (src-size 0) and never stored;
+// the k tail of the last tile is fixed up by fix_k_tail.
+struct TileLoader {
+  const float* a_src;   // A + (m0 + (t>>3)) * lda + 4*(t&7)
+  const float* b_src;   // B + (t>>7) * ldb + n0 + (t&127)
+  int64_t a_step;       // 32 * lda
+  int64_t b_step;       // 2 * ldb
+  int64_t k;
+  uint32_t a_dst, b_dst;
+  int a_kq, b_kpar;
+  uint32_t a_rowmask;   // bit e: row (t>>3) + 32e exists
+  bool b_colok;
+  // A rows not 16-byte aligned (lda % 4 != 0 or a misaligned base): 4-byte copies
+  bool a_vec;
+  const float* a_base;  // A + m0 * lda
+  int64_t a_lda, a_rows;
+  uint32_t a_smem;      // stage-0 A base
+  int tid_;
 
-  __device__ __forceinline__ ALoader(const float* A, int64_t lda_, int64_t m, int64_t k_, int64_t m0, int tid_,
-                                     uint32_t smem_a, bool avec) {
-    const int ra = tid_ >> 3;
-    kq = (tid_ & 7) * 4;
-    step = 32 * lda_;
-    rowmask = 0;
+  __device__ __forceinline__ TileLoader(const float* A, const float* B, const GemmArgs& p, int64_t m0, int64_t n0,
+                                        int tid, const float* smem_base, bool avec = true) {
+    const int ra = tid >> 3;
+    a_kq = (tid & 7) * 4;
+    a_step = 32 * p.lda;
+    a_rowmask = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      if (m0 + ra + 32 * e < m) rowmask |= 1u << e;
-    src = (m0 + ra < m) ? A + (m0 + ra) * lda_ + kq : A;
-    base = A + m0 * lda_;
-    k = k_;
-    lda = lda_;
-    rows = m - m0;
-    dst = smem_a + uint32_t((ra * kFApitch + kq) * 4);
-    smem = smem_a;
-    tid = tid_;
-    vec = avec;
+      if (m0 + ra + 32 * e < p.m) a_rowmask |= 1u << e;
+    a_src = (m0 + ra < p.m) ? A + (m0 + ra) * p.lda + a_kq : A;
+    b_kpar = tid >> 7;
+    const int nn = tid & 127;
+    b_colok = (n0 + nn) < p.n;
+    b_step = 2 * p.ldb;
+    b_src = b_colok ? B + int64_t(b_kpar) * p.ldb + n0 + nn : B;
+    k = p.k;
+    a_dst = smem_u32(smem_base) + uint32_t((ra * kFApitch + a_kq) * 4);
+    a_vec = avec;
+    a_base = A + m0 * p.lda;
+    a_lda = p.lda;
+    a_rows = p.m - m0;
+    a_smem = smem_u32(smem_base);
+    tid_ = tid;
+    b_dst = smem_u32(smem_base + kFAStage) + uint32_t((nn * 2 + b_kpar) * 4);
   }
 
-  __device__ __forceinline__ void load(uint32_t soff, int64_t kt) const {
+  __device__ __forceinline__ void load(int stage, int64_t kt) const {
+    const uint32_t soff = uint32_t(stage) * uint32_t(kFStageFloats * 4);
+    load_a_at(soff, kt);
+    load_b(soff, kt);
+  }
+
+  __device__ __forceinline__ void load_a_at(uint32_t soff, int64_t kt) const {
     const int64_t k0 = kt * kFBK;
-    if (!vec) {
+    const bool interior = k0 + kFBK <= k;
+    if (!a_vec) {
 #pragma unroll
       for (int e = 0; e < (kFBM * kFBK) / kFThreads; ++e) {
-        const int lin = tid + e * kFThreads;
+        const int lin = tid_ + e * kFThreads;
         const int row = lin >> 5, kk = lin & 31;
-        const bool ok = row < rows && k0 + kk < k;
-        cp_async4(smem + soff + uint32_t((row * kFApitch + kk) * 4), ok ? base + row * lda + k0 + kk : base,
+        const bool ok = row < a_rows && k0 + kk < k;
+        cp_async4(a_smem + soff + uint32_t((row * kFApitch + kk) * 4), ok ? a_base + row * a_lda + k0 + kk : a_base,
                   ok ? 4 : 0);
       }
       return;
     }
-    const float* s = src + k0;
-    int bytes = 16;
-    if (k0 + kFBK > k) {
-      const int64_t rem = k - (k0 + kq);
-      bytes = rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0);
-    }
+    {
+      const float* src = a_src + k0;
+      int bytes = 16;
+      if (!interior) {
+        const int64_t rem = k - (k0 + a_kq);
+        bytes = rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0);
+      }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const bool ok = (rowmask >> e) & 1u;
-      cp_async16(dst + soff + uint32_t(e * 32 * kFApitch * 4), ok && bytes ? s : src, ok ? bytes : 0);
-      s += step;
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = (a_rowmask >> e) & 1u;
+        cp_async16(a_dst + soff + uint32_t(e * 32 * kFApitch * 4), ok && bytes ? src : a_src, ok ? bytes : 0);
+        src += a_step;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void load_b(uint32_t soff, int64_t kt) const {
+    const int64_t k0 = kt * kFBK;
+    const bool interior = k0 + kFBK <= k;
+    {
+      const float* src = b_src + k0 * (b_step >> 1);
+      if (interior) {
+        const int bytes = b_colok ? 4 : 0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          cp_async4(b_dst + soff + uint32_t(e * kFBN * 2 * 4), src, bytes);
+          src += b_colok ? b_step : 0;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const bool ok = b_colok && (k0 + b_kpar + 2 * e < k);
+          cp_async4(b_dst + soff + uint32_t(e * kFBN * 2 * 4), ok ? src : b_src, ok ? 4 : 0);
+          src += b_colok ? b_step : 0;
+        }
+      }
     }
   }
 };
 
-// Per-thread staging of the B side of one k-tile (32 k x 128 n) into the
-// k-pair-interleaved layout [k/2][n][2] by 4-byte cp.async: thread t copies
-// column t&127 for k rows (t>>7) + 2e, e = 0..15, so its shared-memory
-// destinations are 1 KiB apart and its sources 2*ldb apart.  Out-of-range
-// columns and k are zero-filled and never stored.
-struct BLoader {
-  const float* src;     // B + (t>>7) * ldb + n0 + (t&127)
-  int64_t step;         // 2 * ldb
-  int64_t k;
-  uint32_t dst;
-  int kpar;
-  bool colok;
-
-  __device__ __forceinline__ BLoader(const float* B, int64_t ldb, int64_t n, int64_t k_, int64_t n0, int tid,
-                                     uint32_t smem_b) {
-    kpar = tid >> 7;
-    const int nn = tid & 127;
-    colok = (n0 + nn) < n;
-    step = 2 * ldb;
-    src = colok ? B + int64_t(kpar) * ldb + n0 + nn : B;
-    k = k_;
-    dst = smem_b + uint32_t((nn * 2 + kpar) * 4);
-  }
-
-  __device__ __forceinline__ void load(uint32_t soff, int64_t kt) const {
+// Re-stream staging of one k-tile into a ring slot (layout of ring_a /
+// ring_b).  16-byte copies when rows are 16-byte aligned, 4-byte copies
+// otherwise; out-of-range elements are zero-filled (the scan masks k >= K).
+struct RingLoader {
+  const float* A;   // row m0 of this batch's A
+  const float* B;   // this batch's B
+  int64_t rows, cols, kdim, lda, ldb, n0;
+  int tid;
+  bool a_vec, b_vec;
+  uint32_t base;
+  __device__ __forceinline__ RingLoader(const float* A_, const float* B_, const GemmArgs& p, int64_t m0, int64_t n0_,
+                                        int tid_, const float* smem_base, bool avec, bool bvec)
+      : A(A_ + m0 * p.lda), B(B_), rows(p.m - m0), cols(p.n - n0_), kdim(p.k), lda(p.lda), ldb(p.ldb), n0(n0_),
+        tid(tid_), a_vec(avec), b_vec(bvec), base(smem_u32(smem_base)) {}
+  __device__ __forceinline__ void load(int slot, int64_t kt) const {
+    const uint32_t sb = base + uint32_t(slot) * uint32_t(kRStageFloats * 4);
     const int64_t k0 = kt * kFBK;
-#ifdef TG_EXP_B16
-    {  // experiment: the cost of four 16-byte copies per thread (wrong layout)
-      const float* b0 = src - kpar * (step >> 1);
-      const uint32_t d0 = dst - uint32_t(((threadIdx.x & 127) * 2 + kpar) * 4);
+    if (a_vec) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int lin = threadIdx.x + e * kFThreads;
-        const int kk = lin >> 5, c = (lin & 31) * 4;
-        cp_async16(d0 + soff + uint32_t((kk * kFBN + c) * 4), b0 + (k0 + kk) * (step >> 1) + c - (threadIdx.x & 127), 16);
-      }
-      return;
-    }
-#endif
-    const float* s = src + k0 * (step >> 1);
-    if (k0 + kFBK <= k) {
-      const int bytes = colok ? 4 : 0;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        cp_async4(dst + soff + uint32_t(e * kFBN * 2 * 4), s, bytes);
-        s += colok ? step : 0;
+      for (int e = 0; e < (kFBM * kFBK / 4) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int r = lin >> 3, kq = (lin & 7) * 4;
+        const int64_t rem = kdim - (k0 + kq);
+        const int bytes = r < rows ? (rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0)) : 0;
+        cp_async16(sb + uint32_t(ring_a(r, kq) * 4), bytes ? A + r * lda + k0 + kq : A, bytes);
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const bool ok = colok && (k0 + kpar + 2 * e < k);
-        cp_async4(dst + soff + uint32_t(e * kFBN * 2 * 4), ok ? s : src, ok ? 4 : 0);
-        s += colok ? step : 0;
+      for (int e = 0; e < (kFBM * kFBK) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int r = lin >> 5, kk = lin & 31;
+        const bool ok = r < rows && k0 + kk < kdim;
+        cp_async4(sb + uint32_t(ring_a(r, kk) * 4), ok ? A + r * lda + k0 + kk : A, ok ? 4 : 0);
+      }
+    }
+    if (b_vec) {
+#pragma unroll
+      for (int e = 0; e < (kFBK * kFBN / 4) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int kk = lin >> 5, c = (lin & 31) * 4;
+        const int64_t rem = cols - c;
+        const int bytes = k0 + kk < kdim ? (rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0)) : 0;
+        cp_async16(sb + uint32_t(ring_b(kk, c) * 4), bytes ? B + (k0 + kk) * ldb + n0 + c : B, bytes);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < (kFBK * kFBN) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
+        const int kk = lin >> 7, c = lin & 127;
+        const bool ok = k0 + kk < kdim && c < cols;
+        cp_async4(sb + uint32_t(ring_b(kk, c) * 4), ok ? B + (k0 + kk) * ldb + n0 + c : B, ok ? 4 : 0);
       }
     }
   }
@@ -236,7 +310,9 @@ __device__ __forceinline__ void fix_k_tail(float* stage, int kvalid, int tid) {
 }
 
 // OUTI: C is int32 (the i32 path computes exactly in f32 on converted
-// operands and converts the result back).
+// operands and converts the result back).  acc_init: accumulator start value
+// (the semiring zero for f32; the reference's integer sentinel for i32 --
+// the sentinel operands themselves are mapped to +-inf by the conversion).
 template <typename CT>
 __device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
   if constexpr (sizeof(CT) == 4 && !std::is_same<CT, float>::value) C[o] = CT(v); else C[o] = v;
@@ -252,7 +328,7 @@ __device__ __forceinline__ void tile_math(const float* stage, int wm, int wn, in
   using Op = FastOps<S>;
   const float* Ap = stage + (wm * 32 + lm) * kFApitch;
   const float* Bp = stage + kFAStage + (wn * 64 + 2 * ln) * 2;
-#pragma unroll kK4Unroll
+#pragma unroll
   for (int k4 = 0; k4 < kFBK; k4 += 4) {
     float4 a[8];
 #pragma unroll
@@ -292,19 +368,21 @@ __device__ __forceinline__ void tile_math(const float* stage, int wm, int wn, in
   }
 }
 
-// Values only (ARGMAX = false) or, for short K, argmax by k-pair tracking
-// (ARGMAX = true): ~2 more instructions per product than values only, but
-// nothing to resolve after the k loop except one reload per output.
-// acc_init: accumulator start value (the semiring zero for f32; the
-// reference's integer sentinel for the i32 path, whose sentinel operands the
-// conversion maps to +-inf).  AVEC: A rows are 16-byte aligned.
-template <int S, bool ARGMAX, bool OUTI = false, bool AVEC = true>
+// PAIR (with ARGMAX, for short K): instead of chunk detection + re-stream,
+// track the winner per k-pair in registers -- after each FADD2/FMNMX3 step a
+// strict compare of the new running value against the old one, and on an
+// improvement the first of the two products that attains it (value bits and
+// index).  ~3 instructions per product instead of ~1, but no re-stream,
+// whose cost per output does not shrink with K.
+// AVEC: A rows are 16-byte aligned (else A is staged by 4-byte copies).
+template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true>
 __global__ void __launch_bounds__(kFThreads, 1)
-fast_f32_kernel(GemmArgs p, float acc_init) {
+fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   using Op = FastOps<S>;
   using CT = typename std::conditional<OUTI, int32_t, float>::type;
   if (gated_off(p)) return;
   extern __shared__ __align__(16) float smem[];
+  unsigned char* sbytes = reinterpret_cast<unsigned char*>(smem);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int lm = lane >> 3, ln = lane & 7;
@@ -320,27 +398,28 @@ fast_f32_kernel(GemmArgs p, float acc_init) {
   const int64_t ktiles = (p.k + kFBK - 1) / kFBK;
   const int kvalid_last = int(p.k - (ktiles - 1) * kFBK);
 
-  const uint32_t sbase = smem_u32(smem);
-  const ALoader la(A, p.lda, p.m, p.k, m0, tid, sbase, AVEC);
-  const BLoader lb(B, p.ldb, p.n, p.k, n0, tid, sbase + kFAStage * 4);
-  constexpr uint32_t kStageBytes = uint32_t(kFStageFloats * 4);
+  const TileLoader ldr(A, B, p, m0, n0, tid, smem, AVEC);
+  uint16_t* cid = reinterpret_cast<uint16_t*>(sbytes + kOffCid);
+  if (ARGMAX && !PAIR) {
+    for (int i = tid; i < kFBM * kFBN; i += kFThreads) cid[i] = kNoChunk;
+  }
 
   float acc[8][8];
-  int32_t pidx[ARGMAX ? 8 : 1][ARGMAX ? 8 : 1];
+  float snap[ARGMAX && !PAIR ? 8 : 1][ARGMAX && !PAIR ? 8 : 1];
+  int32_t pidx[PAIR ? 8 : 1][PAIR ? 8 : 1];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       acc[r][c] = acc_init;
-      if (ARGMAX) pidx[r][c] = -1;
+      if (ARGMAX && !PAIR) snap[r][c] = acc_init;
+      if (PAIR) pidx[r][c] = -1;
     }
 
+  // ------------------------------------------------------------ main loop
 #pragma unroll
   for (int s = 0; s < kFStages - 1; ++s) {
-    if (s < ktiles) {
-      la.load(s * kStageBytes, s);
-      lb.load(s * kStageBytes, s);
-    }
+    if (s < ktiles) ldr.load(s, s);
     cp_async_commit();
   }
   for (int64_t t = 0; t < ktiles; ++t) {
@@ -352,25 +431,40 @@ fast_f32_kernel(GemmArgs p, float acc_init) {
       __syncthreads();
     }
     {
-      const int64_t nt = t + kFStages - 1;
-      if (nt < ktiles) {
-        la.load(uint32_t(nt % kFStages) * kStageBytes, nt);
-        lb.load(uint32_t(nt % kFStages) * kStageBytes, nt);
-      }
+      int64_t nt = t + kFStages - 1;
+      if (nt < ktiles) ldr.load(int(nt % kFStages), nt);
       cp_async_commit();
     }
-    tile_math<S, ARGMAX>(stage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    tile_math<S, PAIR>(stage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    if (ARGMAX && !PAIR && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
+      // chunk boundary: remember the chunk of each output's latest strict improvement
+      const uint16_t chunk = uint16_t(t / tiles_per_chunk);
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (Op::better(acc[r][c], snap[r][c]))
+            cid[(wm * 32 + r * 4 + lm) * kFBN + wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)] = chunk;
+          snap[r][c] = acc[r][c];
+        }
+    }
   }
   cp_async_wait<0>();
 
+  // ------------------------------------------------------------ epilogue
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    const int64_t gr = m0 + wm * 32 + r * 4 + lm;
+    const int lr = wm * 32 + r * 4 + lm;
+    const int64_t gr = m0 + lr;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const int64_t gc = n0 + wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1);
-      if (gr >= p.m || gc >= p.n) continue;
-      if (ARGMAX) {
+      const int lc = wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1);
+      const int64_t gc = n0 + lc;
+      if (gr >= p.m || gc >= p.n) {
+        if (ARGMAX && !PAIR) cid[lr * kFBN + lc] = kNoChunk;   // padding: never resolved
+        continue;
+      }
+      if (PAIR) {
         // pidx: first k of the pair that held the last strict improvement
         // (-1: none, the output is (zero, 0)).  The reference's index is the
         // pair's first k whose product equals the final value; its bits are
@@ -390,13 +484,231 @@ fast_f32_kernel(GemmArgs p, float acc_init) {
         }
         store_c(C, gr * p.ldc + gc, v);
         IDX[gr * p.ldc + gc] = kw;
-      } else {
+      } else if (!ARGMAX) {
         store_c(C, gr * p.ldc + gc, acc[r][c]);
+      } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
+        store_c(C, gr * p.ldc + gc, acc_init);
+        IDX[gr * p.ldc + gc] = 0;
       }
     }
   }
+  if (!ARGMAX || PAIR) return;
+
+  // -------------------------------------------- argmax: bucket by chunk
+  __syncthreads();
+  uint16_t* list = reinterpret_cast<uint16_t*>(sbytes + kOffList);
+  uint16_t* off = reinterpret_cast<uint16_t*>(sbytes + kOffOff);
+  int* cnt = reinterpret_cast<int*>(smem);            // the stages are idle after the k loop
+  int* cursor = cnt + (kFMaxChunks + 1);
+  const int nchunks = int((ktiles + tiles_per_chunk - 1) / tiles_per_chunk);
+  for (int i = tid; i <= nchunks; i += kFThreads) cnt[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
+    const uint16_t ch = cid[i];
+    if (ch != kNoChunk) atomicAdd(&cnt[ch + 1], 1);
+  }
+  __syncthreads();
+  if (warp == 0) {  // inclusive scan of counts: bucket c is list[off[c], off[c+1])
+    int carry = 0;
+    for (int base = 1; base <= nchunks; base += 32) {
+      int i = base + lane;
+      int v = i <= nchunks ? cnt[i] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        int u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
+      }
+      if (i <= nchunks) cnt[i] = v + carry;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i <= nchunks; i += kFThreads) {
+    off[i] = uint16_t(cnt[i]);
+    if (i < nchunks) cursor[i] = cnt[i];
+  }
+  __syncthreads();
+  for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
+    const uint16_t ch = cid[i];
+    if (ch != kNoChunk) list[atomicAdd(&cursor[ch], 1)] = uint16_t(i);
+  }
+  __syncthreads();
+
+  // ---------------------- argmax: re-stream the chunks that own outputs
+  // Every output of chunk c had its last strict improvement in c, so its
+  // final value is the max (min) of its products over c, and its reference
+  // index is the first k of c whose product equals that value.  Tiles of the
+  // owned chunks stream through a kRStages-deep ring (the chunk ids and the
+  // counters are dead now); a chunk is scanned once all its tiles have landed.
+  const RingLoader rl(A, B, p, m0, n0, tid, smem, AVEC, b_vec != 0);
+  auto next_owned = [&](int c) {
+    while (c < nchunks && off[c + 1] == off[c]) ++c;
+    return c;
+  };
+  int ld_chunk = next_owned(0);
+  int64_t ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
+  int64_t issued = 0;
+  auto issue_until = [&](int64_t limit) {
+    while (ld_chunk < nchunks && issued < limit) {
+      rl.load(int(issued % kRStages), ld_tile);
+      cp_async_commit();
+      ++issued;
+      ++ld_tile;
+      if (ld_tile >= int64_t(ld_chunk + 1) * tiles_per_chunk || ld_tile >= ktiles) {
+        ld_chunk = next_owned(ld_chunk + 1);
+        ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
+      }
+    }
+  };
+  issue_until(kRStages);
+  int64_t seq0 = 0;   // ring sequence number of the current chunk's first tile
+  const int grp = tid >> 2, sub = tid & 3;
+  for (int c = next_owned(0); c < nchunks; c = next_owned(c + 1)) {
+    const int64_t t0 = int64_t(c) * tiles_per_chunk;
+    const int nt = int(i64min(tiles_per_chunk, ktiles - t0));
+    const int64_t need = seq0 + nt;
+    if (issued < need) {   // chunks longer than two tiles: make room, then issue the rest
+      __syncthreads();
+      issue_until(need);
+    }
+    const int64_t pending = issued - need;   // groups allowed to stay in flight
+    if (pending >= 4) cp_async_wait<4>();
+    else if (pending == 3) cp_async_wait<3>();
+    else if (pending == 2) cp_async_wait<2>();
+    else if (pending == 1) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();
+    // every thread is past the previous chunk: its ring slots may be refilled
+    issue_until(seq0 + kRStages);
+    const int beg = off[c], end = off[c + 1];
+    const int slot0 = int(seq0 % kRStages);
+    const int klast = int(i64min(kFBK, p.k - (t0 + nt - 1) * kFBK));   // valid k in the chunk's last tile
+    // 64 groups of 4 lanes; lane `sub` owns k = sub, sub+4, ..., sub+28 of
+    // every tile of the chunk.  Pass 1: group max of the products; pass 2:
+    // lowest k whose product equals it.  Trip counts are block-uniform, so
+    // every lane reaches the shuffles.  Each group handles two entries per
+    // round (independent chains for ILP); the products of pass 1 stay in
+    // registers for pass 2.
+    if (nt == 2 && klast == kFBK) {
+      // Full two-tile chunk: no k-range masks; pass 1 is a max3 tree, pass 2
+      // a 16-bit equality mask whose lowest set bit is the lane's first
+      // winning k (bit order = k order).
+      const float* st0 = smem + slot0 * kRStageFloats;
+      const float* st1 = smem + (slot0 + 1 >= kRStages ? slot0 + 1 - kRStages : slot0 + 1) * kRStageFloats;
+      for (int e0 = beg; e0 < end; e0 += 2 * (kFThreads / 4)) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int e = e0 + u * (kFThreads / 4) + grp;
+          const bool act = e < end;
+          const int o = act ? list[e] : 0;
+          const int lr = o >> 7, lc = o & 127;
+          float pv[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pv[i] = Op::mul(st0[ring_a(lr, sub + 4 * i)], st0[ring_b(sub + 4 * i, lc)]);
+            pv[8 + i] = Op::mul(st1[ring_a(lr, sub + 4 * i)], st1[ring_b(sub + 4 * i, lc)]);
+          }
+          float m = Op::red3(Op::red3(Op::red3(pv[0], pv[1], pv[2]), Op::red3(pv[3], pv[4], pv[5]),
+                                      Op::red3(pv[6], pv[7], pv[8])),
+                             Op::red3(Op::red3(pv[9], pv[10], pv[11]), Op::red3(pv[12], pv[13], pv[14]), pv[15]),
+                             pv[15]);
+          float x = __shfl_xor_sync(0xffffffffu, m, 1);
+          m = Op::red3(m, x, x);
+          x = __shfl_xor_sync(0xffffffffu, m, 2);
+          m = Op::red3(m, x, x);
+          unsigned mask = 0;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) mask |= (pv[q] == m) ? (1u << q) : 0u;
+          unsigned kf = 0xFFFFFFFFu;
+          if (mask) {
+            const int q = __ffs(mask) - 1;
+            kf = unsigned(32 * (q >> 3) + sub + 4 * (q & 7));
+          }
+          unsigned first = min(kf, __shfl_xor_sync(0xffffffffu, kf, 1));
+          first = min(first, __shfl_xor_sync(0xffffffffu, first, 2));
+          if (act && first != 0xFFFFFFFFu && kf == first) {
+            const float* st = first >= unsigned(kFBK) ? st1 : st0;
+            const int kk = int(first) & (kFBK - 1);
+            const float v = Op::mul(st[ring_a(lr, kk)], st[ring_b(kk, lc)]);
+            const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
+            store_c(C, gofs, v);
+            IDX[gofs] = int32_t(t0 * kFBK + first);
+          }
+        }
+      }
+      seq0 = need;
+      continue;
+    }
+    constexpr int kE = 2;
+    for (int e0 = beg; e0 < end; e0 += kE * (kFThreads / 4)) {
+      int o[kE];
+      bool active[kE];
+      float pr[kE][4][8];
+      float best[kE];
+#pragma unroll
+      for (int u = 0; u < kE; ++u) {
+        const int e = e0 + u * (kFThreads / 4) + grp;
+        active[u] = e < end;
+        o[u] = active[u] ? list[e] : 0;
+        best[u] = Op::zero();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j < nt) {
+          const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
+          const float* st = smem + slot * kRStageFloats;
+          const int kc = j == nt - 1 ? klast : kFBK;
+#pragma unroll
+          for (int u = 0; u < kE; ++u) {
+            const int lr = o[u] >> 7, lc = o[u] & 127;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              pr[u][j][i] = Op::mul(st[ring_a(lr, sub + 4 * i)], st[ring_b(sub + 4 * i, lc)]);
+              if (sub + 4 * i < kc && Op::better(pr[u][j][i], best[u])) best[u] = pr[u][j][i];
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kE; ++u)
+#pragma unroll
+        for (int d = 1; d < 4; d <<= 1) {
+          const float other = __shfl_xor_sync(0xffffffffu, best[u], d);
+          if (Op::better(other, best[u])) best[u] = other;
+        }
+      unsigned cand[kE], first[kE];
+      float cp[kE];
+#pragma unroll
+      for (int u = 0; u < kE; ++u) { cand[u] = 0xFFFFFFFFu; cp[u] = 0.f; }
+#pragma unroll
+      for (int j = 3; j >= 0; --j) {
+        if (j < nt) {
+          const int kc = j == nt - 1 ? klast : kFBK;
+#pragma unroll
+          for (int u = 0; u < kE; ++u)
+#pragma unroll
+            for (int i = 7; i >= 0; --i)
+              if (sub + 4 * i < kc && pr[u][j][i] == best[u]) {
+                cand[u] = unsigned(j * kFBK + sub + 4 * i);
+                cp[u] = pr[u][j][i];
+              }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kE; ++u) {
+        first[u] = cand[u];
+#pragma unroll
+        for (int d = 1; d < 4; d <<= 1) first[u] = min(first[u], __shfl_xor_sync(0xffffffffu, first[u], d));
+        if (active[u] && first[u] != 0xFFFFFFFFu && cand[u] == first[u]) {
+          const int64_t gofs = (m0 + (o[u] >> 7)) * p.ldc + (n0 + (o[u] & 127));
+          store_c(C, gofs, cp[u]);
+          IDX[gofs] = int32_t(t0 * kFBK + first[u]);
+        }
+      }
+    }
+    seq0 = need;
+  }
+  cp_async_wait<0>();
 }
 
 }  // namespace tg
-
-#include "tg_fast_f32_argmax.cuh"
