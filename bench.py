@@ -243,7 +243,8 @@ CASES = ("backward", "f64", "f64_values", "apsp_step", "minplus_inf", "pipe_rate
 PIPE_VARIANTS = ("pair_fadd2_fmnmx3", "fadd2_alone", "fmnmx3_alone", "fadd_alone", "fmnmx_alone",
                  "fadd_x2_fmnmx3", "fadd2_fmnmx_x2", "fadd_fmnmx", "engine_ktile_body",
                  "engine_ktile_body_with_barrier", "ktile_body_bpair_outer", "ktile_body_two_kpairs",
-                 "ktile_body_two_kpairs_tree", "ktile_body_kquad_swapped", "ktile_body_kquad_aligned")
+                 "ktile_body_two_kpairs_tree", "ktile_body_kquad_swapped", "ktile_body_kquad_aligned",
+                 "pair_b_lds128", "pair_b_lds64", "pair_b_lds128_prefetched")
 
 
 def pipe_rates(blocks_per_sm=(1, 2), iters=20000, variants=PIPE_VARIANTS):
@@ -259,8 +260,9 @@ def pipe_rates(blocks_per_sm=(1, 2), iters=20000, variants=PIPE_VARIANTS):
     for name in variants:
         v = PIPE_VARIANTS.index(name)
         row = {}
-        for occ in (blocks_per_sm if v < 8 else (1,)):
-            it = iters if v < 8 else max(1, iters // 32)
+        body = 8 <= v < 15
+        for occ in ((1,) if body else blocks_per_sm):
+            it = max(1, iters // 32) if body else iters
             r, ms = ctypes.c_double(), ctypes.c_double()
             rc = lib.tg_probe_pipe_rate(v, occ, 256, it, ctypes.byref(r), ctypes.byref(ms))
             if rc != 0:
@@ -527,10 +529,11 @@ def run_engine(args):
         # second denominator: the measured rate of the kernel's own instruction
         # mix (FADD2 + 3-input FMNMX, register-only probe, 8 warps per SM)
         try:
-            mix = pipe_rates(blocks_per_sm=(1,), iters=4000, variants=("pair_fadd2_fmnmx3",))
-            mix = mix["pair_fadd2_fmnmx3"]["warps_per_sm_8"]
+            pr = pipe_rates(blocks_per_sm=(1,), iters=4000, variants=("pair_fadd2_fmnmx3", "pair_b_lds128"))
+            mix = pr["pair_fadd2_fmnmx3"]["warps_per_sm_8"]
+            mix_smem = pr["pair_b_lds128"]["warps_per_sm_8"]
         except Exception:  # the probe library is optional for the contract line
-            mix = None
+            mix = mix_smem = None
         mix_peak = props.multi_processor_count * mix * sm_max * 1e6 if mix else None
         out = {
             "metric": METRIC,
@@ -559,7 +562,13 @@ def run_engine(args):
                          "frac_mix": achieved / mix_peak if mix_peak else None,
                          "mix_basis": (f"measured FADD2 + FMNMX3 issue rate {mix:.1f} products/clk/SM "
                                        f"(bench.py --case pipe_rates) x {props.multi_processor_count} SMs x "
-                                       f"{sm_max:.0f} MHz") if mix else None},
+                                       f"{sm_max:.0f} MHz") if mix else None,
+                         "smem_fed_peak": (props.multi_processor_count * mix_smem * sm_max * 1e6 / 1e12)
+                         if mix_smem else None,
+                         "frac_smem_fed": (achieved / (props.multi_processor_count * mix_smem * sm_max * 1e6))
+                         if mix_smem else None,
+                         "smem_fed_basis": (f"the same pair with its B operands reloaded from shared memory every "
+                                            f"iteration: {mix_smem:.1f} products/clk/SM") if mix_smem else None},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * (M * K + K * N_),
                     "d2h_bytes_per_step": 8 * M * N_, "api": "tropical_gemm.maxplus_matmul_dlpack"},
             "gpu_launches": args.steps,

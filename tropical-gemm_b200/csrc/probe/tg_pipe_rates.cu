@@ -60,6 +60,8 @@ __device__ __forceinline__ float fadd(float a, float b) {
 //  8, 9          the engine's k-tile body from shared memory (below)
 template <int V>
 __global__ void __launch_bounds__(256) pipe_kernel(int iters, long long* stamps, float* sink) {
+  __shared__ __align__(16) float sm[2048];
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x) sm[i] = -1e-3f * float(i % 13 + 1);
   float acc[64];
   const float seed = float(threadIdx.x) * 1e-3f;
 #pragma unroll
@@ -71,10 +73,48 @@ __global__ void __launch_bounds__(256) pipe_kernel(int iters, long long* stamps,
     bs[q] = -1e-3f * float(q + 1);
     B[q] = pk(bs[q], -2e-3f * float(q + 1));
   }
+  float4 pre[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) pre[q] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
   long long t0 = clock64();
   for (int it = 0; it < iters; ++it) {
-    if (V == 0 || V == 5 || V == 6) {
+    if (V >= 15) {
+      // variant 0 with the B pairs reloaded from shared memory every
+      // iteration: 15 by four 16-byte loads, 16 by eight 8-byte loads,
+      // 17 by four 16-byte loads issued one iteration ahead
+      const int base = ((it & 7) * 64 + (threadIdx.x & 7) * 4) % 2048;
+      float4 bq[4];
+      if (V == 15) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bq[q] = *reinterpret_cast<const float4*>(sm + (base + q * 32) % 2048);
+      } else if (V == 16) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 x = *reinterpret_cast<const float2*>(sm + (base + q * 32) % 2048);
+          const float2 y = *reinterpret_cast<const float2*>(sm + (base + q * 32 + 2) % 2048);
+          bq[q] = make_float4(x.x, x.y, y.x, y.y);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bq[q] = pre[q];
+        const int nb = (((it + 1) & 7) * 64 + (threadIdx.x & 7) * 4) % 2048;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) pre[q] = *reinterpret_cast<const float4*>(sm + (nb + q * 32) % 2048);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const unsigned long long A = pk(acc[r * 8], acc[r * 8 + 1]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float lo, hi;
+          upk(fadd2(A, pk(bq[q].x, bq[q].y)), lo, hi);
+          acc[r * 8 + 2 * q] = fmax3(acc[r * 8 + 2 * q], lo, hi);
+          upk(fadd2(A, pk(bq[q].z, bq[q].w)), lo, hi);
+          acc[r * 8 + 2 * q + 1] = fmax3(acc[r * 8 + 2 * q + 1], lo, hi);
+        }
+      }
+    } else if (V == 0 || V == 5 || V == 6) {
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
         const float a0 = acc[r * 8], a1 = acc[r * 8 + 1];
@@ -181,6 +221,8 @@ __global__ void __launch_bounds__(256, 1) body_kernel(int iters, long long* stam
 //  13: B staged as one float4 of four k per column with its two k-pairs swapped,
 //      so each FADD2 pairs A's (x,y) with B's (z,w) registers and vice versa
 //  14: as 13 without the swap (A's (x,y) with B's (x,y))
+//  15-17: variant 0 with its B pairs reloaded from shared memory every
+//      iteration (16-byte loads / 8-byte loads / 16-byte loads one iteration ahead)
 __device__ __forceinline__ void fadd2s(float& lo, float& hi, float a0, float a1, float b0, float b1) {
   tg::FastOps<tg::kMaxPlus>::pair(lo, hi, a0, a1, b0, b1);
 }
@@ -290,13 +332,16 @@ __global__ void __launch_bounds__(256, 1) alt_kernel(int iters, long long* stamp
   }
 }
 
-constexpr int kVariants = 15;
+constexpr int kVariants = 18;
 constexpr int kProducts[kVariants] = {128, 128, 128, 64, 64, 128, 128, 64, 64 * tg::kFBK, 64 * tg::kFBK,
-                                      64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK};
+                                      64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK,
+                                      128, 128, 128};
 
 template <int V>
 cudaError_t launch(int blocks, int threads, int iters, long long* st, float* sink) {
-  if constexpr (V >= 10) {
+  if constexpr (V >= 15) {
+    pipe_kernel<V><<<blocks, threads>>>(iters, st, sink);
+  } else if constexpr (V >= 10) {
     alt_kernel<V><<<blocks, threads, tg::kFStageFloats * 4>>>(iters, st, sink);
   } else if constexpr (V >= 8) {
     body_kernel<V><<<blocks, threads, tg::kFStageFloats * 4>>>(iters, st, sink);
@@ -330,7 +375,8 @@ extern "C" int tg_probe_pipe_rate(int variant, int blocks_per_sm, int threads, i
     using L = cudaError_t (*)(int, int, int, long long*, float*);
     const L table[kVariants] = {launch<0>, launch<1>, launch<2>, launch<3>, launch<4>,
                                 launch<5>, launch<6>, launch<7>, launch<8>, launch<9>,
-                                launch<10>, launch<11>, launch<12>, launch<13>, launch<14>};
+                                launch<10>, launch<11>, launch<12>, launch<13>, launch<14>,
+                                launch<15>, launch<16>, launch<17>};
     if (variant < 0 || variant >= kVariants) variant = 0;
     const L fn = table[variant];
     e = fn(blocks, threads, 8, st, sink);   // warm-up
