@@ -8,6 +8,7 @@
 #pragma once
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include "tg_internal.h"
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
@@ -39,7 +40,7 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
   const bool pair = ARGMAX && P.g.k <= kPairMaxK;
   const bool avec = (reinterpret_cast<uintptr_t>(P.g.a) & 15) == 0 && P.g.lda % 4 == 0 &&
                     (P.batch == 1 || P.g.sa % 4 == 0);
-  using KernT = void (*)(tg::GemmArgs, int, int, float);
+  using KernT = void (*)(tg::GemmArgs, int, int, float, const CUtensorMap, const CUtensorMap, int);
   KernT kern;
   int variant;
   if constexpr (OUTI) {   // the i32 path stages padded, aligned copies
@@ -71,7 +72,17 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
     g.b = static_cast<const float*>(g.b) + b0 * g.sb;
     g.c = static_cast<float*>(g.c) + b0 * g.sc;
     if (ARGMAX) g.argmax = g.argmax + b0 * g.sc;
-    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec, acc_init);
+    // the chunk re-stream by TMA when A and B rows and batch strides are 16-byte aligned
+    CUtensorMap ta, tb;
+    std::memset(&ta, 0, sizeof(ta));
+    std::memset(&tb, 0, sizeof(tb));
+    int use_tma = 0;
+    if (ARGMAX && !pair && avec && b_vec && (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(g.b) & 15) == 0 && (nb == 1 || (g.sa % 4 == 0 && g.sb % 4 == 0)))
+      use_tma = encode_tma_f32(g.a, g.k, g.m, g.lda, nb, g.sa, tg::kFBK, tg::kFBM, &ta) &&
+                encode_tma_f32(g.b, g.n, g.k, g.ldb, nb, g.sb, 32, tg::kFBK, &tb);
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec, acc_init, ta, tb,
+                                                                                       use_tma);
     tg_status s = check_launch("fast_f32_kernel launch");
     if (s != TG_OK) return s;
   }

@@ -32,6 +32,7 @@
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
 #include <type_traits>
+#include <cuda.h>
 
 namespace tg {
 
@@ -55,7 +56,8 @@ constexpr int kRStageFloats = kRAFloats + kFBK * kFBN;     // + B slot: 32 k x 1
 constexpr size_t kOffCid = kFSmemValues;
 constexpr size_t kOffList = size_t(kRStages) * kRStageFloats * 4;
 constexpr size_t kOffOff = kOffList + size_t(kFBM * kFBN) * 2;
-constexpr size_t kFSmemArgmax = kOffOff + size_t(kFMaxChunks + 1) * 2;
+constexpr size_t kOffBar = (kOffOff + size_t(kFMaxChunks + 1) * 2 + 7) & ~size_t(7);   // ring mbarriers (TMA)
+constexpr size_t kFSmemArgmax = kOffBar + size_t(kRStages) * 8;
 static_assert(kOffCid + size_t(kFBM * kFBN) * 2 <= kOffList, "chunk ids overlap the list");
 static_assert(size_t(2 * (kFMaxChunks + 1)) * 4 <= kOffCid, "bucket counters overlap the chunk ids");
 static_assert(kFSmemArgmax <= 232448, "argmax kernel exceeds shared memory");
@@ -66,8 +68,8 @@ static_assert(kFBM * kFBN <= 65535, "u16 bucket offsets");
 // the scan's column reads (4 lanes on consecutive k of one output, 8 outputs
 // per warp) spread over the banks.
 __device__ __forceinline__ int ring_a(int r, int k) { return r * kFBK + ((((k >> 2) ^ (r & 7)) << 2) | (k & 3)); }
-__device__ __forceinline__ int ring_b(int k, int n) {
-  return kRAFloats + k * kFBN + ((((n >> 2) ^ (k & 7)) << 2) | (n & 3));
+__device__ __forceinline__ int ring_b(int k, int n) {   // four 32-column boxes of 128-byte rows
+  return kRAFloats + (n >> 5) * (kFBK * 32) + k * 32 + (((((n >> 2) & 7) ^ (k & 7)) << 2) | (n & 3));
 }
 
 template <int S> struct FastOps;
@@ -127,6 +129,34 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, int byt
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" :: "n"(N));
+}
+
+// ---- TMA re-stream of the ring (bulk tensor copies completing on an
+// mbarrier per ring slot; no multicast).  The ring's A slot (128 rows x 32 k,
+// 128-byte rows) and B slot (four 32 k x 32 n boxes) use the hardware's
+// 128-byte swizzle, which is the XOR pattern of ring_a / ring_b below.
+__device__ __forceinline__ void mbar_init(uint32_t bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" :: "r"(bar), "r"(count));
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
+      :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
+}
+// Waits for phase `parity` of the barrier, giving up after a bounded number
+// of polls (returns false then; the caller marks its outputs).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 22); ++i) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+    if (done) return true;
+  }
+  return false;
 }
 
 // Per-thread staging of k-tiles into one pipeline stage, with every address
@@ -377,7 +407,8 @@ __device__ __forceinline__ void tile_math(const float* stage, int wm, int wn, in
 // AVEC: A rows are 16-byte aligned (else A is staged by 4-byte copies).
 template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true>
 __global__ void __launch_bounds__(kFThreads, 1)
-fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
+fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, const __grid_constant__ CUtensorMap tma_a,
+                const __grid_constant__ CUtensorMap tma_b, int use_tma) {
   using Op = FastOps<S>;
   using CT = typename std::conditional<OUTI, int32_t, float>::type;
   if (gated_off(p)) return;
@@ -548,10 +579,32 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
   int ld_chunk = next_owned(0);
   int64_t ld_tile = int64_t(ld_chunk) * tiles_per_chunk;
   int64_t issued = 0;
+  // TMA ring: slot base 1024-byte aligned for the 128-byte swizzle
+  const bool tma = use_tma != 0 && (smem_u32(smem) & 1023) == 0;
+  const uint32_t bars = smem_u32(sbytes + kOffBar);
+  if (tma && tid == 0) {
+    for (int s2 = 0; s2 < kRStages; ++s2) mbar_init(bars + 8 * s2, 1);
+    fence_proxy_async();
+  }
+  if (tma) __syncthreads();
   auto issue_until = [&](int64_t limit) {
+    if (tma && tid == 0) fence_proxy_async();   // the slots' earlier generic accesses come first
     while (ld_chunk < nchunks && issued < limit) {
-      rl.load(int(issued % kRStages), ld_tile);
-      cp_async_commit();
+      if (tma) {
+        if (tid == 0) {
+          const int slot = int(issued % kRStages);
+          const uint32_t sb = smem_u32(smem + slot * kRStageFloats), bar = bars + 8 * slot;
+          mbar_expect_tx(bar, uint32_t(kRStageFloats * 4));
+          tma_load3(sb, &tma_a, int(ld_tile * kFBK), int(m0), int(batch), bar);
+#pragma unroll
+          for (int j = 0; j < kFBN / 32; ++j)
+            tma_load3(sb + uint32_t((kRAFloats + j * kFBK * 32) * 4), &tma_b, int(n0) + 32 * j, int(ld_tile * kFBK),
+                      int(batch), bar);
+        }
+      } else {
+        rl.load(int(issued % kRStages), ld_tile);
+        cp_async_commit();
+      }
       ++issued;
       ++ld_tile;
       if (ld_tile >= int64_t(ld_chunk + 1) * tiles_per_chunk || ld_tile >= ktiles) {
@@ -571,13 +624,26 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init) {
       __syncthreads();
       issue_until(need);
     }
-    const int64_t pending = issued - need;   // groups allowed to stay in flight
-    if (pending >= 4) cp_async_wait<4>();
-    else if (pending == 3) cp_async_wait<3>();
-    else if (pending == 2) cp_async_wait<2>();
-    else if (pending == 1) cp_async_wait<1>();
-    else cp_async_wait<0>();
+    bool landed = true;
+    if (tma) {
+      for (int64_t q = seq0; q < need; ++q)
+        landed = mbar_wait(bars + 8 * uint32_t(q % kRStages), uint32_t((q / kRStages) & 1)) && landed;
+    } else {
+      const int64_t pending = issued - need;   // groups allowed to stay in flight
+      if (pending >= 4) cp_async_wait<4>();
+      else if (pending == 3) cp_async_wait<3>();
+      else if (pending == 2) cp_async_wait<2>();
+      else if (pending == 1) cp_async_wait<1>();
+      else cp_async_wait<0>();
+    }
     __syncthreads();
+    if (!__syncthreads_and(landed)) {   // a copy never arrived: mark the chunk's outputs, stop
+      for (int e = off[c] + tid; e < off[c + 1]; e += kFThreads) {
+        const int o = list[e];
+        IDX[(m0 + (o >> 7)) * p.ldc + (n0 + (o & 127))] = -2;
+      }
+      return;
+    }
     // every thread is past the previous chunk: its ring slots may be refilled
     issue_until(seq0 + kRStages);
     const int beg = off[c], end = off[c + 1];

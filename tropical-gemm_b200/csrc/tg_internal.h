@@ -5,6 +5,7 @@
 // parallel); tg_backward.cu holds the backward dispatch.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include "../../include/tropical_gemm_b200.h"
 #include "tg_generic.cuh"
@@ -31,6 +32,13 @@ cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st);
 void scratch_free(void* p, cudaStream_t st);
 
 bool fast_f32_ok(const Problem& P);
+
+// A 3-D f32 tensor map (inner, rows, batch) with a (box_inner x box_rows x 1)
+// box, 128-byte swizzle and zero fill out of bounds, for the TMA re-stream.
+// False when the driver entry point is missing or the layout is not
+// encodable (16-byte aligned base and strides are the caller's check).
+bool encode_tma_f32(const void* base, int64_t inner, int64_t rows, int64_t ld, int64_t batch, int64_t bstride,
+                    uint32_t box_inner, uint32_t box_rows, CUtensorMap* out);
 
 // One semiring's dispatch over the four dtypes (canonical row-major problem).
 template <int S> tg_status dispatch(tg_dtype dtype, const Problem& P, cudaStream_t st);
