@@ -97,3 +97,50 @@ def test_backward_matches_reference_kernels():
     torch.cuda.synchronize()
     assert torch.allclose(ga, ga_r, rtol=1e-6, atol=1e-5)
     assert torch.allclose(gb, gb_r, rtol=1e-6, atol=1e-5)
+
+
+def _apsp_matrix(n, seed):
+    """BASELINE config 4 input: 5 % density, weights 1..1000, missing edges =
+    the reference's i32 infinity (46340), zero diagonal."""
+    g = torch.Generator(device=dev()).manual_seed(seed)
+    w = torch.randint(1, 1001, (n, n), generator=g, device=dev(), dtype=torch.int32)
+    d = torch.where(torch.rand((n, n), generator=g, device=dev()) < 0.05, w,
+                    torch.full_like(w, 46340))
+    d.fill_diagonal_(0)
+    return d
+
+
+def test_config4_apsp_squaring_16384_matches_reference_kernel():
+    """One full-size APSP squaring (MinPlus i32 + argmax, n = 16384): ties are
+    frequent, so the index tie-break is exercised at scale."""
+    d = _apsp_matrix(16384, 4)
+    c, am = N.gemm("minplus", d, d, True)
+    cr, amr = ref_rowmajor("minplus", d, d, True)
+    torch.cuda.synchronize()
+    assert torch.equal(c, cr) and torch.equal(am, amr)
+    del c, am, cr, amr
+    # the second squaring starts from distances, not edge weights
+    d2, _ = N.gemm("minplus", d, d, False)
+    c, am = N.gemm("minplus", d2, d2, True)
+    cr, amr = ref_rowmajor("minplus", d2, d2, True)
+    assert torch.equal(c, cr) and torch.equal(am, amr)
+
+
+@pytest.mark.parametrize("case", ["maxplus_f32_argmax", "maxmul_f64_values"])
+def test_config5_row_block_matches_reference_kernel(case):
+    """One rank's row block of BASELINE config 5 (4096 of M = 32768 rows,
+    N = 32768, K = 8192): MaxPlus f32 + argmax on N(0,1) and MaxMul f64
+    values on U[0,1)."""
+    g = torch.Generator(device=dev()).manual_seed(2)
+    if case == "maxplus_f32_argmax":
+        a = torch.randn((4096, 8192), generator=g, device=dev())
+        b = torch.randn((8192, 32768), generator=g, device=dev())
+        c, am = N.gemm("maxplus", a, b, True)
+        cr, amr = ref_rowmajor("maxplus", a, b, True)
+        assert _eq(c, cr) and torch.equal(am, amr)
+    else:
+        a = torch.rand((4096, 8192), generator=g, device=dev(), dtype=torch.float64)
+        b = torch.rand((8192, 32768), generator=g, device=dev(), dtype=torch.float64)
+        c, _ = N.gemm("maxmul", a, b, False)
+        cr, _ = ref_rowmajor("maxmul", a, b, False)
+        assert _eq(c, cr)
