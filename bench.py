@@ -225,7 +225,13 @@ def extras(dev):
         tropical_maxplus_matmul_batched(ab, bb).sum().backward()
 
     ms = _time_ms(step, reps=10, warm=3)
-    res["batched_autograd_fwd_bwd_64x512x256x512"] = {"ms": ms, "fwd_ops_per_s": 64 * 512 * 256 * 512 / (ms * 1e-3)}
+    ms_f = _time_ms(lambda: Nat.gemm_batched("maxplus", ab.detach(), bb.detach(), True), reps=10, warm=3)
+    _, amb = Nat.gemm_batched("maxplus", ab.detach(), bb.detach(), True)
+    gcb = torch.ones((64, 512, 512), device=dev)
+    ms_b = _time_ms(lambda: (Nat.backward("maxplus", True, gcb, amb, 256),
+                             Nat.backward("maxplus", False, gcb, amb, 256)), reps=10, warm=3)
+    res["batched_autograd_fwd_bwd_64x512x256x512"] = {"ms": ms, "fwd_ops_per_s": 64 * 512 * 256 * 512 / (ms * 1e-3),
+                                                       "fwd_kernel_ms": ms_f, "bwd_kernels_ms": ms_b}
     # 4: one APSP squaring, MinPlus i32, n = 16384, 5% density, weights 1..1000, missing = 46340
     n = 16384
     mask = rng.random((n, n)) < 0.05
@@ -235,6 +241,19 @@ def extras(dev):
     ms = _time_ms(lambda: Nat.gemm("minplus", td, td, True), reps=2)
     res["apsp_minplus_i32_argmax_16384_one_squaring"] = {"ops_per_s": float(n) ** 3 / (ms * 1e-3), "ms": ms,
                                                          "14_squarings_s": 14 * ms / 1e3}
+    del td
+    # 5: one rank's row block of the sharded config (4096 of 32768 rows)
+    gg = torch.Generator(device=dev).manual_seed(2)
+    a5 = torch.randn((4096, 8192), generator=gg, device=dev)
+    b5 = torch.randn((8192, 32768), generator=gg, device=dev)
+    ms = _time_ms(lambda: Nat.gemm("maxplus", a5, b5, True), reps=2)
+    res["5_row_block_4096x32768x8192_maxplus_f32_argmax"] = {"ms": ms, "ops_per_s": 4096.0 * 32768 * 8192 / (ms * 1e-3)}
+    del a5, b5
+    a5 = torch.rand((4096, 8192), generator=gg, device=dev, dtype=torch.float64)
+    b5 = torch.rand((8192, 32768), generator=gg, device=dev, dtype=torch.float64)
+    ms = _time_ms(lambda: Nat.gemm("maxmul", a5, b5, False), reps=2)
+    res["5_row_block_4096x32768x8192_maxmul_f64_values"] = {"ms": ms,
+                                                            "ops_per_s": 4096.0 * 32768 * 8192 / (ms * 1e-3)}
     return res
 
 
@@ -605,6 +624,101 @@ def run_engine(args):
         dist.destroy_process_group()
 
 
+def _ev_ms(fn, reps=3, warm=1):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def reference_gpu_configs(dev):
+    """The reference's CUDA kernels (oracle/_ref, compiled from its .cu with
+    nvcc -O3 for sm_100a) on each BASELINE configuration, same inputs as the
+    engine's extras: ms per launch and tropical ops/s."""
+    from oracle.ref_gpu import ref_lib, ref_rowmajor
+    L = ref_lib()
+    if L is None:
+        return {"unavailable": "reference kernels not built (oracle/_ref)"}
+    res = {"kernels": "crates/tropical-gemm-cuda/kernels/tropical_gemm.cu, reference launch geometry"}
+    rng = np.random.default_rng(1)
+    # 2a: MaxPlus f32 + argmax 8192^3 (and values only)
+    a_np, b_np = make_inputs(8192)
+    a = torch.from_numpy(a_np).to(dev)
+    b = torch.from_numpy(b_np).to(dev)
+    ms = _ev_ms(lambda: ref_rowmajor("maxplus", a, b, True))
+    res["2a_maxplus_f32_argmax_8192"] = {"ms": ms, "ops_per_s": 8192.0 ** 3 / (ms * 1e-3)}
+    ms = _ev_ms(lambda: ref_rowmajor("maxplus", a, b, False))
+    res["2a_maxplus_f32_values_8192"] = {"ms": ms, "ops_per_s": 8192.0 ** 3 / (ms * 1e-3)}
+    del a, b
+    # 2b: MinPlus f32 + argmax, U[0,100) with 90 % +inf
+    mats = []
+    for _ in range(2):
+        v = (100 * rng.random((8192, 8192))).astype(np.float32)
+        v[rng.random((8192, 8192)) < 0.9] = np.inf
+        mats.append(torch.from_numpy(v).to(dev))
+    ms = _ev_ms(lambda: ref_rowmajor("minplus", mats[0], mats[1], True))
+    res["2b_minplus_f32_argmax_90pct_inf_8192"] = {"ms": ms, "ops_per_s": 8192.0 ** 3 / (ms * 1e-3)}
+    del mats
+    # 3: batched forward (reference batched argmax kernel) + backward as the
+    # reference's torch path does it (pytorch.py:386-403: two scatter_add_)
+    g = torch.Generator().manual_seed(0)
+    ab = torch.randn((64, 512, 256), generator=g).to(dev)
+    bb = torch.randn((64, 256, 512), generator=g).to(dev)
+    cb = torch.empty((64, 512, 512), device=dev)
+    amb = torch.empty((64, 512, 512), dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def fwd():
+        rc = L.ref_gemm_batched_argmax_f32(0, 64, 512, 512, 256, bb.data_ptr(), ab.data_ptr(), cb.data_ptr(),
+                                           amb.data_ptr(), 256 * 512, 512 * 256, 512 * 512, st)
+        assert rc == 0
+
+    ms_f = _ev_ms(fwd, reps=10, warm=3)
+    gc = torch.ones((64, 512, 512), device=dev)
+    am64 = amb.long()
+
+    def bwd():
+        ga = torch.zeros((64, 512, 256), device=dev)
+        ga.scatter_add_(2, am64, gc)
+        gbt = torch.zeros((64, 512, 256), device=dev)
+        gbt.scatter_add_(2, am64.transpose(1, 2), gc.transpose(1, 2))
+        return ga, gbt.transpose(1, 2)
+
+    ms_b = _ev_ms(bwd, reps=10, warm=3)
+    res["3_batched_64x512x256x512"] = {"fwd_ms": ms_f, "fwd_ops_per_s": 64 * 512 * 256 * 512 / (ms_f * 1e-3),
+                                       "bwd_ms_torch_scatter": ms_b, "fwd_bwd_ms": ms_f + ms_b}
+    del ab, bb, cb, amb, gc, am64
+    # 4: one APSP squaring, MinPlus i32 + argmax, n = 16384
+    n = 16384
+    mask = rng.random((n, n)) < 0.05
+    d = np.where(mask, rng.integers(1, 1001, (n, n)), 46340).astype(np.int32)
+    np.fill_diagonal(d, 0)
+    td = torch.from_numpy(d).to(dev)
+    ms = _ev_ms(lambda: ref_rowmajor("minplus", td, td, True), reps=1)
+    res["4_apsp_minplus_i32_argmax_16384_one_squaring"] = {"ms": ms, "ops_per_s": float(n) ** 3 / (ms * 1e-3),
+                                                           "14_squarings_s": 14 * ms / 1e3}
+    del td
+    # 5: one rank's row block of the sharded config (4096 of 32768 rows)
+    gg = torch.Generator(device=dev).manual_seed(2)
+    a5 = torch.randn((4096, 8192), generator=gg, device=dev)
+    b5 = torch.randn((8192, 32768), generator=gg, device=dev)
+    ms = _ev_ms(lambda: ref_rowmajor("maxplus", a5, b5, True), reps=1)
+    res["5_row_block_4096x32768x8192_maxplus_f32_argmax"] = {"ms": ms, "ops_per_s": 4096.0 * 32768 * 8192 / (ms * 1e-3)}
+    del a5, b5
+    a5 = torch.rand((4096, 8192), generator=gg, device=dev, dtype=torch.float64)
+    b5 = torch.rand((8192, 32768), generator=gg, device=dev, dtype=torch.float64)
+    ms = _ev_ms(lambda: ref_rowmajor("maxmul", a5, b5, False), reps=1)
+    res["5_row_block_4096x32768x8192_maxmul_f64_values"] = {"ms": ms,
+                                                            "ops_per_s": 4096.0 * 32768 * 8192 / (ms * 1e-3)}
+    return res
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -633,28 +747,11 @@ def run_reference(args):
                                    "built here), all host threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    # The reference's own CUDA kernel on this GPU (built from its sources).
+    # The reference's own CUDA kernels on this GPU (built from its sources),
+    # on every BASELINE configuration.
     try:
         if torch.cuda.is_available():
-            from oracle.ref_gpu import ref_lib, ref_rowmajor
-            if ref_lib() is not None:
-                dev = torch.device("cuda", 0)
-                a_np, b_np = make_inputs(M)
-                a = torch.from_numpy(a_np).to(dev)
-                b = torch.from_numpy(b_np).to(dev)
-                for _ in range(2):
-                    ref_rowmajor("maxplus", a, b, True)
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                reps = 3
-                for _ in range(reps):
-                    ref_rowmajor("maxplus", a, b, True)
-                e1.record()
-                torch.cuda.synchronize()
-                ms = e0.elapsed_time(e1) / reps
-                out["reference_gpu"] = {"value": float(M) * N_ * K / (ms * 1e-3), "unit": UNIT, "ms_per_launch": ms,
-                                        "kernel": "tropical_maxplus_f32_nn_with_argmax (reference source, nvcc sm_100a)"}
+            out["reference_gpu"] = reference_gpu_configs(torch.device("cuda", 0))
     except Exception as e:  # the CPU figure above is the arm's value; this key is informational
         out["reference_gpu"] = {"error": str(e)[:200]}
     print(json.dumps(out), flush=True)
