@@ -89,6 +89,25 @@ tg_status tg_gemm_strided_batched(tg_semiring semiring, tg_dtype dtype, tg_layou
                                   int32_t* argmax,
                                   void* stream);
 
+/* Accumulating f32 GEMM over one K slice: every output starts from its
+ * current value in C (and keeps its argmax) unless a product of this slice
+ * strictly beats it; a winning k is written as k_offset + k.  Computing
+ * K = [0, k1) with tg_gemm and then [k1, k2), ... with this call (A's and
+ * B's slices, k_offset = slice start) gives results identical to one
+ * tg_gemm over the whole K, so a caller can overlap the transfer of B's next
+ * K slice with the arithmetic of the current one.  f32 only (others:
+ * TG_ERR_UNSUPPORTED); argmax may be null (values only).  No reference
+ * counterpart: the reference computes whole products in one launch
+ * (kernels.rs:388-434); this is the building block of the pipelined sharded
+ * GEMM. */
+tg_status tg_gemm_accumulate(tg_semiring semiring, tg_layout layout,
+                             int64_t m, int64_t n, int64_t k,
+                             const float* a, int64_t lda,
+                             const float* b, int64_t ldb,
+                             float* c, int64_t ldc,
+                             int32_t* argmax, int32_t k_offset,
+                             void* stream);
+
 /* Broadcast callback for tg_sharded_gemm: make the `bytes` bytes of device
  * memory at `buf` equal to rank `root`'s copy, enqueued on `stream` (for
  * example ncclBroadcast on the caller's communicator, so the library links no

@@ -82,6 +82,29 @@ WORKER = textwrap.dedent('''
     CB = D.gather_batches(cb, bs); AMB = D.gather_batches(amb, bs)
     cb0, amb0 = O.gemm_batched("minplus", ab, bb)
     assert np.array_equal(CB.numpy(), cb0) and np.array_equal(AMB.numpy(), amb0)
+    # the K-pipelined broadcast: slice 0 by an ordinary GEMM, later slices
+    # merged in place with the strict first-k-wins rule and global indices;
+    # small integers make ties across slice boundaries frequent
+    ai = rng.integers(-4, 5, (m, 200)).astype(np.float32)
+    bi_full = rng.integers(-4, 5, (200, n)).astype(np.float32)
+    b2 = torch.from_numpy(bi_full.copy()) if rank == 0 else torch.zeros((200, n))
+    def acc(semi, aa, bb, c, am, off):
+        v, i = O.gemm(semi, np.ascontiguousarray(aa.numpy()), np.ascontiguousarray(bb.numpy()), True)
+        v, i = torch.from_numpy(v), torch.from_numpy(i)
+        win = v > c if semi != "minplus" else v < c
+        c[win] = v[win]
+        am[win] = i[win] + off
+    def first(semi, aa, bb, wa):
+        c, am = O.gemm(semi, np.ascontiguousarray(aa.numpy()), np.ascontiguousarray(bb.numpy()), wa)
+        return torch.from_numpy(c), torch.from_numpy(am)
+    s, e = D.shard_rows(m, world, rank)
+    for semi in ("maxplus", "minplus"):
+        c, am = D.pipelined_sharded_matmul(semi, torch.from_numpy(ai[s:e]), b2, chunks=3, first=first, accumulate=acc)
+        assert torch.equal(b2, torch.from_numpy(bi_full))
+        C = D.gather_rows(c, m); AM = D.gather_rows(am, m)
+        c0, am0 = O.gemm(semi, ai, bi_full)
+        assert np.array_equal(C.numpy(), c0) and np.array_equal(AM.numpy(), am0), semi
+    assert D.k_slices(200, 3) == [(0, 128), (128, 192), (192, 200)]
     dist.destroy_process_group()
     print("rank", rank, "ok")
 ''')

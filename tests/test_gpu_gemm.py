@@ -347,3 +347,37 @@ def test_i32_argmax_beyond_the_chunk_limit():
                                           ti.data_ptr(), torch.cuda.current_stream().cuda_stream))
             c, am = tc.cpu().numpy(), ti.cpu().numpy()
         assert np.array_equal(c, c0) and np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("k,cuts,with_argmax", [(2000, (700, 1600), True), (900, (300,), True),
+                                                (1500, (512, 1000), False), (3000, (64, 2900), True)])
+def test_accumulate_over_k_slices_equals_one_pass(semi, k, cuts, with_argmax):
+    """K sliced at `cuts`: tg_gemm on the first slice, tg_gemm_accumulate on
+    the rest (A's column slices passed with its full leading dimension) gives
+    the one-pass result bit for bit.  Small-integer values make ties across
+    slice boundaries frequent: the earlier slice must keep them."""
+    g = torch.Generator(device=dev()).manual_seed(k)
+    m, n = 300, 260
+    a = torch.randint(-6, 7, (m, k), generator=g, device=dev()).float()
+    b = torch.randint(-6, 7, (k, n), generator=g, device=dev()).float()
+    if semi == "maxmul":
+        a, b = a.abs(), b.abs()
+    c_ref, am_ref = N.gemm(semi, a, b, with_argmax)
+    bounds = [0, *cuts, k]
+    c, am = N.gemm(semi, a[:, : bounds[1]], b[: bounds[1]].contiguous(), with_argmax)
+    for s0, s1 in zip(bounds[1:-1], bounds[2:]):
+        N.gemm_accumulate(semi, a[:, s0:s1], b[s0:s1].contiguous(), c, am, s0)
+    torch.cuda.synchronize()
+    assert torch.equal(c.view(torch.int32), c_ref.view(torch.int32))
+    if with_argmax:
+        assert torch.equal(am, am_ref)
+        _, am_or = oracle(semi, a.cpu().numpy(), b.cpu().numpy())
+        assert np.array_equal(am.cpu().numpy(), am_or)
+
+
+def test_accumulate_rejects_other_dtypes():
+    a = torch.zeros((4, 4), dtype=torch.float64, device=dev())
+    c = torch.zeros((4, 4), dtype=torch.float64, device=dev())
+    with pytest.raises(ValueError):
+        N.gemm_accumulate("maxplus", a, a, c, None, 0)

@@ -242,6 +242,36 @@ tg_status tg_backward_b(tg_semiring semiring, tg_dtype dtype, tg_layout layout, 
                        grad_b, ldb, stride_b, accumulate, stream);
 }
 
+tg_status tg_gemm_accumulate(tg_semiring semiring, tg_layout layout, int64_t m, int64_t n, int64_t k, const float* a,
+                             int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc, int32_t* argmax,
+                             int32_t k_offset, void* stream) {
+  clear_error();
+  if (semiring < TG_MAXPLUS || semiring > TG_MAXMUL) return fail(TG_ERR_INVALID_ARGUMENT, "unknown semiring %d", int(semiring));
+  if (layout != TG_ROW_MAJOR && layout != TG_COL_MAJOR) return fail(TG_ERR_INVALID_ARGUMENT, "unknown layout %d", int(layout));
+  if (m < 0 || n < 0 || k < 0) return fail(TG_ERR_INVALID_ARGUMENT, "negative size (m=%lld n=%lld k=%lld)", (long long)m, (long long)n, (long long)k);
+  if (k_offset < 0 || int64_t(k_offset) + k >= (int64_t(1) << 31)) return fail(TG_ERR_INVALID_ARGUMENT, "k_offset %d out of range", int(k_offset));
+  if (m == 0 || n == 0 || k == 0) return TG_OK;   // an empty slice changes nothing
+  if (!c || !a || !b) return fail(TG_ERR_INVALID_ARGUMENT, "null operand");
+  const bool row = layout == TG_ROW_MAJOR;
+  const int64_t need_lda = row ? k : m, need_ldb = row ? n : k, need_ldc = row ? n : m;
+  if (lda < need_lda) return fail(TG_ERR_DIMENSION_MISMATCH, "lda=%lld < %lld", (long long)lda, (long long)need_lda);
+  if (ldb < need_ldb) return fail(TG_ERR_DIMENSION_MISMATCH, "ldb=%lld < %lld", (long long)ldb, (long long)need_ldb);
+  if (ldc < need_ldc) return fail(TG_ERR_DIMENSION_MISMATCH, "ldc=%lld < %lld", (long long)ldc, (long long)need_ldc);
+  Problem P;
+  P.batch = 1;
+  P.g = row ? tg::GemmArgs{m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, argmax}
+            : tg::GemmArgs{n, m, k, b, ldb, 0, a, lda, 0, c, ldc, 0, argmax};
+  P.g.accumulate = 1;
+  P.g.k_offset = k_offset;
+  if (!fast_f32_ok(P)) return fail(TG_ERR_UNSUPPORTED, "K=%lld is beyond the accumulating kernel's range", (long long)k);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (semiring) {
+    case TG_MAXPLUS: return dispatch<tg::kMaxPlus>(TG_F32, P, st);
+    case TG_MINPLUS: return dispatch<tg::kMinPlus>(TG_F32, P, st);
+    default: return dispatch<tg::kMaxMul>(TG_F32, P, st);
+  }
+}
+
 tg_status tg_sharded_gemm(tg_semiring semiring, tg_dtype dtype, int64_t m_local, int64_t n, int64_t k,
                           const void* a_local, int64_t lda, void* b, int64_t ldb, void* c_local, int64_t ldc,
                           int32_t* argmax_local, int root, tg_broadcast_fn bcast, void* bcast_ctx, void* stream) {

@@ -443,7 +443,13 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       acc[r][c] = acc_init;
-      if (ARGMAX && !PAIR) snap[r][c] = acc_init;
+      if constexpr (!OUTI) {
+        if (p.accumulate) {   // start from the current C (a previous K slice's result)
+          const int64_t gr = m0 + wm * 32 + r * 4 + lm, gc = n0 + wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1);
+          if (gr < p.m && gc < p.n) acc[r][c] = C[gr * p.ldc + gc];
+        }
+      }
+      if (ARGMAX && !PAIR) snap[r][c] = acc[r][c];
       if (PAIR) pidx[r][c] = -1;
     }
 
@@ -503,6 +509,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
         const int32_t kg = pidx[r][c];
         float v = acc_init;
         int32_t kw = 0;
+        if (kg < 0 && p.accumulate) continue;   // nothing beat the previous slices: keep C and argmax
         if (kg >= 0) {
           const float lo = Op::mul(A[gr * p.lda + kg], B[int64_t(kg) * p.ldb + gc]);
           if (lo == acc[r][c] || kg + 1 >= p.k) {
@@ -514,10 +521,10 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
           }
         }
         store_c(C, gr * p.ldc + gc, v);
-        IDX[gr * p.ldc + gc] = kw;
+        IDX[gr * p.ldc + gc] = kw + (kg >= 0 ? p.k_offset : 0);
       } else if (!ARGMAX) {
         store_c(C, gr * p.ldc + gc, acc[r][c]);
-      } else if (cid[lr * kFBN + lc] == kNoChunk) {   // nothing beat the zero: (zero, index 0)
+      } else if (cid[lr * kFBN + lc] == kNoChunk && !p.accumulate) {   // nothing beat the zero: (zero, index 0)
         store_c(C, gr * p.ldc + gc, acc_init);
         IDX[gr * p.ldc + gc] = 0;
       }
@@ -698,7 +705,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
             const float v = Op::mul(st[ring_a(lr, kk)], st[ring_b(kk, lc)]);
             const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
             store_c(C, gofs, v);
-            IDX[gofs] = int32_t(t0 * kFBK + first);
+            IDX[gofs] = int32_t(t0 * kFBK + first) + p.k_offset;
           }
         }
       }
@@ -768,7 +775,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
         if (active[u] && first[u] != 0xFFFFFFFFu && cand[u] == first[u]) {
           const int64_t gofs = (m0 + (o[u] >> 7)) * p.ldc + (n0 + (o[u] & 127));
           store_c(C, gofs, cp[u]);
-          IDX[gofs] = int32_t(t0 * kFBK + first[u]);
+          IDX[gofs] = int32_t(t0 * kFBK + first[u]) + p.k_offset;
         }
       }
     }

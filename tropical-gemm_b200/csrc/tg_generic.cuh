@@ -27,6 +27,12 @@ struct GemmArgs {
   // a host synchronisation.
   const int* gate = nullptr;
   int gate_run_if_set = 0;
+  // Accumulate (f32 fast kernels only): every output starts from its current
+  // C value (and keeps its argmax unless a product strictly beats it); a
+  // winning k is reported as k_offset + k.  Lets a K-sliced problem be
+  // computed slice by slice with results identical to one pass.
+  int accumulate = 0;
+  int32_t k_offset = 0;
 };
 
 __device__ __forceinline__ bool gated_off(const GemmArgs& p) {

@@ -10,6 +10,7 @@ import ctypes
 import os
 
 import torch
+from typing import Optional
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libtropical_gemm_b200.so")
@@ -52,6 +53,8 @@ def lib() -> ctypes.CDLL:
         L.tg_gemm_strided_batched.argtypes = [i32, i32, i32, i64, i64, i64, i64, vp, i64, i64, vp, i64, i64,
                                               vp, i64, i64, i32p, vp]
         L.tg_gemm_strided_batched.restype = i32
+        L.tg_gemm_accumulate.argtypes = [i32, i32, i64, i64, i64, vp, i64, vp, i64, vp, i64, i32p, i32, vp]
+        L.tg_gemm_accumulate.restype = i32
         for fn in (L.tg_backward_a, L.tg_backward_b):
             fn.argtypes = [i32, i32, i32, i64, i64, i64, i64, vp, i64, i64, i32p, vp, i64, i64, vp, i64, i64,
                            i32, vp]
@@ -128,16 +131,52 @@ def gemm(semiring: str, a: torch.Tensor, b: torch.Tensor, with_argmax: bool = Tr
     """Row-major C = A (x) B for 2-D CUDA tensors; returns (C, argmax int32 or None)."""
     _validate_pair(a, b, batched=False)
     _require_cuda(a, b)
-    a = a.contiguous()
+    a = _rows(a)
     b = b.contiguous()
     m, k = a.shape
     n = b.shape[1]
     c = torch.empty((m, n), dtype=a.dtype, device=a.device)
     am = torch.empty((m, n), dtype=torch.int32, device=a.device) if with_argmax else None
     with torch.cuda.device(a.device):
-        check(lib().tg_gemm(SEMIRINGS[semiring], DTYPES[a.dtype], ROW_MAJOR, m, n, k, a.data_ptr(), k, b.data_ptr(),
-                            n, c.data_ptr(), n, am.data_ptr() if am is not None else None, _stream(a)))
+        check(lib().tg_gemm(SEMIRINGS[semiring], DTYPES[a.dtype], ROW_MAJOR, m, n, k, a.data_ptr(), _ld(a),
+                            b.data_ptr(), n, c.data_ptr(), n, am.data_ptr() if am is not None else None, _stream(a)))
     return c, am
+
+
+def _rows(a: torch.Tensor) -> torch.Tensor:
+    """`a` itself when its rows are contiguous (a column slice of a row-major
+    matrix, for instance); a contiguous copy otherwise."""
+    return a if a.dim() == 2 and a.stride(1) == 1 and a.stride(0) >= max(1, a.shape[1]) else a.contiguous()
+
+
+def _ld(a: torch.Tensor) -> int:
+    return max(1, a.stride(0)) if a.shape[0] > 1 else max(1, a.shape[1])
+
+
+def gemm_accumulate(semiring: str, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor,
+                    argmax: Optional[torch.Tensor], k_offset: int) -> None:
+    """In place over one K slice (f32, row-major): every output of `c`
+    (and `argmax`) is replaced where a product of A[:, slice] (x) B[slice, :]
+    strictly beats it; winning indices are k_offset + k.  Starting from
+    gemm() over the first slice, the slices in ascending order give exactly
+    gemm() over the whole K."""
+    _validate_pair(a, b, batched=False)
+    _require_cuda(a, b)
+    if a.dtype != torch.float32:
+        raise ValueError("gemm_accumulate is defined for f32")
+    m, k = a.shape
+    n = b.shape[1]
+    if tuple(c.shape) != (m, n) or not c.is_contiguous() or c.dtype != torch.float32:
+        raise ValueError("C must be a contiguous f32 (m, n) tensor")
+    if argmax is not None and (tuple(argmax.shape) != (m, n) or not argmax.is_contiguous()
+                               or argmax.dtype != torch.int32):
+        raise ValueError("argmax must be a contiguous int32 (m, n) tensor")
+    a = _rows(a)
+    b = b.contiguous()
+    with torch.cuda.device(a.device):
+        check(lib().tg_gemm_accumulate(SEMIRINGS[semiring], ROW_MAJOR, m, n, k, a.data_ptr(), _ld(a), b.data_ptr(), n,
+                                       c.data_ptr(), n, argmax.data_ptr() if argmax is not None else None,
+                                       int(k_offset), _stream(a)))
 
 
 def gemm_batched(semiring: str, a: torch.Tensor, b: torch.Tensor, with_argmax: bool = True):

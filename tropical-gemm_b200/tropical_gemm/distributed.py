@@ -65,6 +65,56 @@ def sharded_matmul(semiring: str, a_local: torch.Tensor, b: torch.Tensor, src: i
     return fn(semiring, a_local, b, with_argmax)
 
 
+def k_slices(k: int, chunks: int, align: int = 64):
+    """[start, stop) bounds of `chunks` ascending K slices (multiples of
+    `align` except the last), as even as the alignment allows."""
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
+    units = (k + align - 1) // align
+    chunks = max(1, min(chunks, units))
+    base, extra = divmod(units, chunks)
+    bounds, u = [0], 0
+    for i in range(chunks):
+        u += base + (1 if i < extra else 0)
+        bounds.append(min(k, u * align))
+    return [(a, b) for a, b in zip(bounds, bounds[1:]) if b > a]
+
+
+def pipelined_sharded_matmul(semiring: str, a_local: torch.Tensor, b: torch.Tensor, src: int = 0, group=None,
+                             with_argmax: bool = True, chunks: int = 4,
+                             first: Optional[Callable] = None, accumulate: Optional[Callable] = None):
+    """sharded_matmul with the broadcast of B pipelined along K: B's K slices
+    (contiguous row blocks of the row-major K x N buffer) go out as
+    asynchronous broadcasts, and slice i is multiplied while slice i+1 is on
+    the wire.  Slice 0 is an ordinary GEMM; each later slice updates C and
+    argmax in place where one of its products strictly beats them, with the
+    global k as index, so the result is bit-identical to one pass over the
+    whole K (the reference's strict, first-k-wins rule).
+
+    `first(semiring, a, b, with_argmax)` and
+    `accumulate(semiring, a, b, c, argmax, k_offset)` default to the engine's
+    gemm and gemm_accumulate (f32)."""
+    first = first or N.gemm
+    accumulate = accumulate or N.gemm_accumulate
+    k = b.shape[0]
+    if k == 0 or a_local.shape[1] != k:
+        broadcast_b(b, src=src, group=group)
+        return first(semiring, a_local, b, with_argmax)
+    spans = k_slices(k, chunks)
+    works = [dist.broadcast(b[spans[0][0]:spans[0][1]], src=src, group=group, async_op=True)]
+    c = am = None
+    for i, (s0, s1) in enumerate(spans):
+        if i + 1 < len(spans):   # next slice on the wire while this one computes
+            n0, n1 = spans[i + 1]
+            works.append(dist.broadcast(b[n0:n1], src=src, group=group, async_op=True))
+        works[i].wait()
+        if i == 0:
+            c, am = first(semiring, a_local[:, s0:s1], b[s0:s1], with_argmax)
+        else:
+            accumulate(semiring, a_local[:, s0:s1], b[s0:s1], c, am, s0)
+    return c, am
+
+
 def gather_rows(x_local: torch.Tensor, m: int, group=None) -> torch.Tensor:
     """All-gather row blocks (as produced by shard_rows) into the full matrix."""
     world = dist.get_world_size(group)
