@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(256, 1) body_kernel(int iters, long long* stam
   long long t0 = clock64();
   for (int it = 0; it < iters; ++it) {
     if (V == 9) __syncthreads();
-    tg::tile_math<tg::kMaxPlus, false>(stage, warp >> 1, warp & 1, lane >> 3, lane & 7, acc, unused, 0);
+    tg::tile_math<tg::kMaxPlus, false>(stage, stage + tg::kFAStage, warp >> 1, warp & 1, lane >> 3, lane & 7, acc, unused, 0);
   }
   __syncthreads();
   long long t1 = clock64();

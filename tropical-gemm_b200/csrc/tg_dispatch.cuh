@@ -34,22 +34,23 @@ constexpr int64_t kPairMaxK = 1024;
 
 template <int S, bool ARGMAX, bool OUTI = false>
 tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
-  const size_t smem = ARGMAX ? tg::kFSmemArgmax : tg::kFSmemValues;
-  // variant: argmax by chunk re-stream or by k-pair tracking (short K);
+  // variant: argmax by chunk re-stream or by k-pair tracking (short K; with
+  // B's panel resident in shared memory up to K = 256);
   // A staged by 16-byte copies when every batch's A rows are 16-byte aligned
   const bool pair = ARGMAX && P.g.k <= kPairMaxK;
+  const bool panel = !OUTI && pair && P.g.k <= tg::kPanelMaxK;
+  const size_t smem = panel ? tg::kFSmemPanel : (ARGMAX && !pair ? tg::kFSmemArgmax : tg::kFSmemValues);
   const bool avec = (reinterpret_cast<uintptr_t>(P.g.a) & 15) == 0 && P.g.lda % 4 == 0 &&
                     (P.batch == 1 || P.g.sa % 4 == 0);
   using KernT = void (*)(tg::GemmArgs, int, int, float, const CUtensorMap, const CUtensorMap, int);
   KernT kern;
-  int variant;
   if constexpr (OUTI) {   // the i32 path stages padded, aligned copies
     kern = pair ? tg::fast_f32_kernel<S, ARGMAX, OUTI, true> : tg::fast_f32_kernel<S, ARGMAX, OUTI, false>;
-    variant = pair ? 1 : 0;
   } else {
-    if (pair) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true> : tg::fast_f32_kernel<S, ARGMAX, false, true, false>;
+    if (panel) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true, true>
+                           : tg::fast_f32_kernel<S, ARGMAX, false, true, false, true>;
+    else if (pair) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true> : tg::fast_f32_kernel<S, ARGMAX, false, true, false>;
     else kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, false, true> : tg::fast_f32_kernel<S, ARGMAX, false, false, false>;
-    variant = (pair ? 1 : 0) + (avec ? 0 : 2);
   }
   {
     tg_status s = ensure_smem(reinterpret_cast<const void*>(kern), smem);

@@ -353,11 +353,12 @@ __device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
 // per output, the first k of the k-pair that held the last strict
 // improvement (kbase = the tile's first k).
 template <int S, bool PAIR>
-__device__ __forceinline__ void tile_math(const float* stage, int wm, int wn, int lm, int ln, float (&acc)[8][8],
-                                          int32_t (&pidx)[PAIR ? 8 : 1][PAIR ? 8 : 1], int64_t kbase) {
+__device__ __forceinline__ void tile_math(const float* a_stage, const float* b_stage, int wm, int wn, int lm, int ln,
+                                          float (&acc)[8][8], int32_t (&pidx)[PAIR ? 8 : 1][PAIR ? 8 : 1],
+                                          int64_t kbase) {
   using Op = FastOps<S>;
-  const float* Ap = stage + (wm * 32 + lm) * kFApitch;
-  const float* Bp = stage + kFAStage + (wn * 64 + 2 * ln) * 2;
+  const float* Ap = a_stage + (wm * 32 + lm) * kFApitch;
+  const float* Bp = b_stage + (wn * 64 + 2 * ln) * 2;
 #pragma unroll
   for (int k4 = 0; k4 < kFBK; k4 += 4) {
     float4 a[8];
@@ -405,7 +406,15 @@ __device__ __forceinline__ void tile_math(const float* stage, int wm, int wn, in
 // index).  ~3 instructions per product instead of ~1, but no re-stream,
 // whose cost per output does not shrink with K.
 // AVEC: A rows are 16-byte aligned (else A is staged by 4-byte copies).
-template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true>
+// BPANEL (PAIR, K <= kPanelMaxK): B's whole 128-column panel stays resident
+// in shared memory (each k-tile's B lands in its own panel slice, A alone
+// cycles through the stages), so the epilogue reloads the winning k-pair of
+// B from shared memory instead of scattered global reads.
+constexpr int kPanelMaxK = 256;
+constexpr size_t kFSmemPanel = size_t(kFStages) * kFAStage * 4 + size_t(kPanelMaxK) * kFBN * 4;
+static_assert(kFSmemPanel <= 232448, "B-panel kernel exceeds shared memory");
+
+template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true, bool BPANEL = false>
 __global__ void __launch_bounds__(kFThreads, 1)
 fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b, int use_tma) {
@@ -454,25 +463,35 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
     }
 
   // ------------------------------------------------------------ main loop
+  // stage layout: [A | B] per stage, or (BPANEL) three A stages then the B panel
+  auto load_tile = [&](int stg, int64_t kt) {
+    if constexpr (BPANEL) {
+      ldr.load_a_at(uint32_t(stg) * uint32_t(kFAStage * 4), kt);
+      ldr.load_b(uint32_t((kFStages - 1) * kFAStage + int(kt) * kFBStage) * 4u, kt);
+    } else {
+      ldr.load(stg, kt);
+    }
+  };
 #pragma unroll
   for (int s = 0; s < kFStages - 1; ++s) {
-    if (s < ktiles) ldr.load(s, s);
+    if (s < ktiles) load_tile(s, s);
     cp_async_commit();
   }
   for (int64_t t = 0; t < ktiles; ++t) {
     cp_async_wait<kFStages - 2>();
     __syncthreads();
-    float* stage = smem + (t % kFStages) * kFStageFloats;
+    float* stage = smem + (t % kFStages) * (BPANEL ? kFAStage : kFStageFloats);
+    const float* bstage = BPANEL ? smem + kFStages * kFAStage + t * kFBStage : stage + kFAStage;
     if (t == ktiles - 1 && kvalid_last < kFBK) {
       fix_k_tail<S>(stage, kvalid_last, tid);
       __syncthreads();
     }
     {
       int64_t nt = t + kFStages - 1;
-      if (nt < ktiles) ldr.load(int(nt % kFStages), nt);
+      if (nt < ktiles) load_tile(int(nt % kFStages), nt);
       cp_async_commit();
     }
-    tile_math<S, PAIR>(stage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    tile_math<S, PAIR>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
     if (ARGMAX && !PAIR && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
       // chunk boundary: remember the chunk of each output's latest strict improvement
       const uint16_t chunk = uint16_t(t / tiles_per_chunk);
@@ -511,12 +530,22 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
         int32_t kw = 0;
         if (kg < 0 && p.accumulate) continue;   // nothing beat the previous slices: keep C and argmax
         if (kg >= 0) {
-          const float lo = Op::mul(A[gr * p.lda + kg], B[int64_t(kg) * p.ldb + gc]);
+          float b0, b1 = 0.f;
+          if constexpr (BPANEL) {   // k-pair of column lc in the resident panel ([k/2][n][2])
+            const float2 bb = *reinterpret_cast<const float2*>(
+                smem + kFStages * kFAStage + (kg >> 1) * (kFBN * 2) + (wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)) * 2);
+            b0 = bb.x;
+            b1 = bb.y;
+          } else {
+            b0 = B[int64_t(kg) * p.ldb + gc];
+            if (kg + 1 < p.k) b1 = B[int64_t(kg + 1) * p.ldb + gc];
+          }
+          const float lo = Op::mul(A[gr * p.lda + kg], b0);
           if (lo == acc[r][c] || kg + 1 >= p.k) {
             v = lo;
             kw = kg;
           } else {
-            v = Op::mul(A[gr * p.lda + kg + 1], B[int64_t(kg + 1) * p.ldb + gc]);
+            v = Op::mul(A[gr * p.lda + kg + 1], b1);
             kw = kg + 1;
           }
         }
