@@ -9,7 +9,6 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
-#include <cstdlib>
 #include "tg_internal.h"
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
@@ -33,16 +32,6 @@ __global__ void fill_zero_kernel(T* c, int32_t* idx, int64_t m, int64_t n, int64
 
 constexpr int64_t kPairMaxK = 1024;
 
-// TG_ARGMAX_TILE128=1 in the environment keeps the 128 x 128 argmax geometry
-// (for measuring the two against each other).
-inline bool tg_geo64_disabled() {
-  static const bool off = [] {
-    const char* v = std::getenv("TG_ARGMAX_TILE128");
-    return v && v[0] == '1';
-  }();
-  return off;
-}
-
 template <int S, bool ARGMAX, bool OUTI = false>
 tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
   // variant: argmax by chunk re-stream or by k-pair tracking (short K; with
@@ -50,15 +39,7 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
   // A staged by 16-byte copies when every batch's A rows are 16-byte aligned
   const bool pair = ARGMAX && P.g.k <= kPairMaxK;
   const bool panel = !OUTI && pair && P.g.k <= tg::kPanelMaxK;
-  const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
-  int tpc = 2;
-  while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
-  // chunk argmax: 64 x 128 tiles, two CTAs per SM (one CTA's re-stream runs
-  // beside the other's k loop) while two-tile chunks fit its 3-slot ring
-  const bool half = ARGMAX && !pair && !OUTI && tpc == 2 && !tg_geo64_disabled();
-  const int bm = half ? 64 : 128, threads = half ? 128 : tg::kFThreads;
-  const size_t smem = panel ? tg::kFSmemPanel
-                            : (ARGMAX && !pair ? (half ? tg::Geo64::SmemArgmax : tg::kFSmemArgmax) : tg::kFSmemValues);
+  const size_t smem = panel ? tg::kFSmemPanel : (ARGMAX && !pair ? tg::kFSmemArgmax : tg::kFSmemValues);
   const bool avec = (reinterpret_cast<uintptr_t>(P.g.a) & 15) == 0 && P.g.lda % 4 == 0 &&
                     (P.batch == 1 || P.g.sa % 4 == 0);
   using KernT = void (*)(tg::GemmArgs, int, int, float, const CUtensorMap, const CUtensorMap, int);
@@ -69,19 +50,20 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
     if (panel) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true, true>
                            : tg::fast_f32_kernel<S, ARGMAX, false, true, false, true>;
     else if (pair) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, true, true> : tg::fast_f32_kernel<S, ARGMAX, false, true, false>;
-    else if (half) kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, false, true, false, 64>
-                               : tg::fast_f32_kernel<S, ARGMAX, false, false, false, false, 64>;
     else kern = avec ? tg::fast_f32_kernel<S, ARGMAX, false, false, true> : tg::fast_f32_kernel<S, ARGMAX, false, false, false>;
   }
   {
     tg_status s = ensure_smem(reinterpret_cast<const void*>(kern), smem);
     if (s != TG_OK) return s;
   }
+  const int64_t ktiles = (P.g.k + tg::kFBK - 1) / tg::kFBK;
+  int tpc = 2;
   const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
                      (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
+  while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
   // (Short K: the re-stream costs as much per output as at long K, so the
   // argmax is tracked per k-pair in registers instead; measured crossover K ~ 1024-1536.)
-  const int64_t gx = (P.g.m + bm - 1) / bm;
+  const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;
   const int64_t gy = (P.g.n + tg::kFBN - 1) / tg::kFBN;
   if (gx > 0x7fffffff || gy > 65535) return fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
   for (int64_t b0 = 0; b0 < P.batch; b0 += 65535) {
@@ -98,10 +80,10 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
     int use_tma = 0;
     if (ARGMAX && !pair && avec && b_vec && (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(g.b) & 15) == 0 && (nb == 1 || (g.sa % 4 == 0 && g.sb % 4 == 0)))
-      use_tma = encode_tma_f32(g.a, g.k, g.m, g.lda, nb, g.sa, tg::kFBK, uint32_t(bm), &ta) &&
+      use_tma = encode_tma_f32(g.a, g.k, g.m, g.lda, nb, g.sa, tg::kFBK, tg::kFBM, &ta) &&
                 encode_tma_f32(g.b, g.n, g.k, g.ldb, nb, g.sb, 32, tg::kFBK, &tb);
-    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), unsigned(threads), smem, st>>>(g, tpc, b_vec, acc_init, ta,
-                                                                                             tb, use_tma);
+    kern<<<dim3(unsigned(gx), unsigned(gy), unsigned(nb)), tg::kFThreads, smem, st>>>(g, tpc, b_vec, acc_init, ta, tb,
+                                                                                       use_tma);
     tg_status s = check_launch("fast_f32_kernel launch");
     if (s != TG_OK) return s;
   }

@@ -63,44 +63,13 @@ static_assert(size_t(2 * (kFMaxChunks + 1)) * 4 <= kOffCid, "bucket counters ove
 static_assert(kFSmemArgmax <= 232448, "argmax kernel exceeds shared memory");
 static_assert(kFBM * kFBN <= 65535, "u16 bucket offsets");
 
-// Tile geometry of the fast kernels: BM rows x 128 columns per CTA, NT
-// threads (8x8 outputs each), and the argmax kernel's shared-memory map for
-// it.  128 x 128 with 256 threads is the default (one CTA per SM); the
-// argmax kernel also runs 64 x 128 with 128 threads, two CTAs per SM, so one
-// CTA's re-stream overlaps the other's k loop.
-template <int BM_, int NT_>
-struct FGeo {
-  static constexpr int BM = BM_, NT = NT_;
-  static constexpr int KPS = NT / 128;                       // B k rows per loader pass
-  static constexpr int AStage = BM * kFApitch;
-  static constexpr int StageFloats = AStage + kFBStage;
-  static constexpr size_t SmemValues = size_t(kFStages) * StageFloats * 4;
-  static constexpr int RStages = BM == 128 ? 6 : 3;          // re-stream ring slots
-  static constexpr int RAFloats = BM * kFBK;
-  static constexpr int RStageFloats = RAFloats + kFBK * kFBN;
-  static constexpr size_t OffCid = SmemValues;
-  static constexpr size_t RingBytes = size_t(RStages) * RStageFloats * 4;
-  static constexpr size_t OffList = RingBytes > OffCid + size_t(BM * kFBN) * 2 ? RingBytes
-                                                                                : OffCid + size_t(BM * kFBN) * 2;
-  static constexpr size_t OffOff = OffList + size_t(BM * kFBN) * 2;
-  static constexpr size_t OffBar = (OffOff + size_t(kFMaxChunks + 1) * 2 + 7) & ~size_t(7);
-  static constexpr size_t SmemArgmax = OffBar + size_t(RStages) * 8;
-  static_assert(NT == 2 * BM && (NT == 256 || NT == 128), "supported geometries: 128x128/256, 64x128/128");
-  static_assert(size_t(2 * (kFMaxChunks + 1)) * 4 <= OffCid, "bucket counters overlap the chunk ids");
-  static_assert(SmemArgmax <= (BM == 128 ? 232448u : 113664u), "argmax kernel exceeds shared memory");
-};
-using Geo128 = FGeo<128, 256>;
-using Geo64 = FGeo<64, 128>;
-static_assert(Geo128::SmemArgmax == kFSmemArgmax && Geo128::OffList == kOffList, "default geometry map");
-
 // Ring-slot element positions.  Rows keep their natural length (no padding);
 // instead the 16-byte groups of a row are XOR-swizzled by the row index, so
 // the scan's column reads (4 lanes on consecutive k of one output, 8 outputs
 // per warp) spread over the banks.
 __device__ __forceinline__ int ring_a(int r, int k) { return r * kFBK + ((((k >> 2) ^ (r & 7)) << 2) | (k & 3)); }
-template <int RAF = kRAFloats>
 __device__ __forceinline__ int ring_b(int k, int n) {   // four 32-column boxes of 128-byte rows
-  return RAF + (n >> 5) * (kFBK * 32) + k * 32 + (((((n >> 2) & 7) ^ (k & 7)) << 2) | (n & 3));
+  return kRAFloats + (n >> 5) * (kFBK * 32) + k * 32 + (((((n >> 2) & 7) ^ (k & 7)) << 2) | (n & 3));
 }
 
 template <int S> struct FastOps;
@@ -191,26 +160,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Per-thread staging of k-tiles into one pipeline stage, with every address
-// term that does not depend on the tile precomputed once per CTA (G = tile
-// geometry; figures below for 128 x 128 with 256 threads).
-//  A: BM rows x 32 k as 16-byte cp.async; thread t copies rows
-//     (t>>3) + (NT/8)e, e = 0..3, at k offset 4*(t&7).
+// term that does not depend on the tile precomputed once per CTA.
+//  A: 128 rows x 32 k as 16-byte cp.async; thread t copies rows
+//     (t>>3) + 32e, e = 0..3, at k offset 4*(t&7).
 //  B: 32 k x 128 n as 4-byte cp.async into the k-pair-interleaved layout;
-//     thread t copies column t&127 for k rows (t>>7) + KPS*e (KPS = NT/128),
-//     so its sources are KPS*ldb apart.
+//     thread t copies column t&127 for rows (t>>7) + 2e, e = 0..15, so its
+//     shared-memory destinations are 1 KiB apart and its sources 2*ldb apart.
 // Out-of-range rows/columns are zero-filled (src-size 0) and never stored;
 // the k tail of the last tile is fixed up by fix_k_tail.
-template <class G = Geo128>
 struct TileLoader {
-  static constexpr int RS = G::NT / 8;   // A rows per pass
   const float* a_src;   // A + (m0 + (t>>3)) * lda + 4*(t&7)
   const float* b_src;   // B + (t>>7) * ldb + n0 + (t&127)
-  int64_t a_step;       // RS * lda
-  int64_t b_step;       // KPS * ldb
+  int64_t a_step;       // 32 * lda
+  int64_t b_step;       // 2 * ldb
   int64_t k;
   uint32_t a_dst, b_dst;
   int a_kq, b_kpar;
-  uint32_t a_rowmask;   // bit e: row (t>>3) + RS*e exists
+  uint32_t a_rowmask;   // bit e: row (t>>3) + 32e exists
   bool b_colok;
   // A rows not 16-byte aligned (lda % 4 != 0 or a misaligned base): 4-byte copies
   bool a_vec;
@@ -223,16 +189,16 @@ struct TileLoader {
                                         int tid, const float* smem_base, bool avec = true) {
     const int ra = tid >> 3;
     a_kq = (tid & 7) * 4;
-    a_step = RS * p.lda;
+    a_step = 32 * p.lda;
     a_rowmask = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      if (m0 + ra + RS * e < p.m) a_rowmask |= 1u << e;
+      if (m0 + ra + 32 * e < p.m) a_rowmask |= 1u << e;
     a_src = (m0 + ra < p.m) ? A + (m0 + ra) * p.lda + a_kq : A;
     b_kpar = tid >> 7;
     const int nn = tid & 127;
     b_colok = (n0 + nn) < p.n;
-    b_step = G::KPS * p.ldb;
+    b_step = 2 * p.ldb;
     b_src = b_colok ? B + int64_t(b_kpar) * p.ldb + n0 + nn : B;
     k = p.k;
     a_dst = smem_u32(smem_base) + uint32_t((ra * kFApitch + a_kq) * 4);
@@ -242,11 +208,11 @@ struct TileLoader {
     a_rows = p.m - m0;
     a_smem = smem_u32(smem_base);
     tid_ = tid;
-    b_dst = smem_u32(smem_base + G::AStage) + uint32_t((nn * 2 + b_kpar) * 4);
+    b_dst = smem_u32(smem_base + kFAStage) + uint32_t((nn * 2 + b_kpar) * 4);
   }
 
   __device__ __forceinline__ void load(int stage, int64_t kt) const {
-    const uint32_t soff = uint32_t(stage) * uint32_t(G::StageFloats * 4);
+    const uint32_t soff = uint32_t(stage) * uint32_t(kFStageFloats * 4);
     load_a_at(soff, kt);
     load_b(soff, kt);
   }
@@ -256,8 +222,8 @@ struct TileLoader {
     const bool interior = k0 + kFBK <= k;
     if (!a_vec) {
 #pragma unroll
-      for (int e = 0; e < (G::BM * kFBK) / G::NT; ++e) {
-        const int lin = tid_ + e * G::NT;
+      for (int e = 0; e < (kFBM * kFBK) / kFThreads; ++e) {
+        const int lin = tid_ + e * kFThreads;
         const int row = lin >> 5, kk = lin & 31;
         const bool ok = row < a_rows && k0 + kk < k;
         cp_async4(a_smem + soff + uint32_t((row * kFApitch + kk) * 4), ok ? a_base + row * a_lda + k0 + kk : a_base,
@@ -275,7 +241,7 @@ struct TileLoader {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const bool ok = (a_rowmask >> e) & 1u;
-        cp_async16(a_dst + soff + uint32_t(e * RS * kFApitch * 4), ok && bytes ? src : a_src, ok ? bytes : 0);
+        cp_async16(a_dst + soff + uint32_t(e * 32 * kFApitch * 4), ok && bytes ? src : a_src, ok ? bytes : 0);
         src += a_step;
       }
     }
@@ -284,23 +250,20 @@ struct TileLoader {
   __device__ __forceinline__ void load_b(uint32_t soff, int64_t kt) const {
     const int64_t k0 = kt * kFBK;
     const bool interior = k0 + kFBK <= k;
-    constexpr int NB = kFBK / G::KPS;   // copies per thread
     {
-      const float* src = b_src + k0 * (b_step / G::KPS);
+      const float* src = b_src + k0 * (b_step >> 1);
       if (interior) {
         const int bytes = b_colok ? 4 : 0;
 #pragma unroll
-        for (int e = 0; e < NB; ++e) {
-          const int kk = G::KPS * e;   // k row (beyond b_kpar) of this copy
-          cp_async4(b_dst + soff + uint32_t(((kk >> 1) * kFBN * 2 + (kk & 1)) * 4), src, bytes);
+        for (int e = 0; e < 16; ++e) {
+          cp_async4(b_dst + soff + uint32_t(e * kFBN * 2 * 4), src, bytes);
           src += b_colok ? b_step : 0;
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < NB; ++e) {
-          const int kk = G::KPS * e;
-          const bool ok = b_colok && (k0 + b_kpar + kk < k);
-          cp_async4(b_dst + soff + uint32_t(((kk >> 1) * kFBN * 2 + (kk & 1)) * 4), ok ? src : b_src, ok ? 4 : 0);
+        for (int e = 0; e < 16; ++e) {
+          const bool ok = b_colok && (k0 + b_kpar + 2 * e < k);
+          cp_async4(b_dst + soff + uint32_t(e * kFBN * 2 * 4), ok ? src : b_src, ok ? 4 : 0);
           src += b_colok ? b_step : 0;
         }
       }
@@ -311,7 +274,6 @@ struct TileLoader {
 // Re-stream staging of one k-tile into a ring slot (layout of ring_a /
 // ring_b).  16-byte copies when rows are 16-byte aligned, 4-byte copies
 // otherwise; out-of-range elements are zero-filled (the scan masks k >= K).
-template <class G = Geo128>
 struct RingLoader {
   const float* A;   // row m0 of this batch's A
   const float* B;   // this batch's B
@@ -324,12 +286,12 @@ struct RingLoader {
       : A(A_ + m0 * p.lda), B(B_), rows(p.m - m0), cols(p.n - n0_), kdim(p.k), lda(p.lda), ldb(p.ldb), n0(n0_),
         tid(tid_), a_vec(avec), b_vec(bvec), base(smem_u32(smem_base)) {}
   __device__ __forceinline__ void load(int slot, int64_t kt) const {
-    const uint32_t sb = base + uint32_t(slot) * uint32_t(G::RStageFloats * 4);
+    const uint32_t sb = base + uint32_t(slot) * uint32_t(kRStageFloats * 4);
     const int64_t k0 = kt * kFBK;
     if (a_vec) {
 #pragma unroll
-      for (int e = 0; e < (G::BM * kFBK / 4) / G::NT; ++e) {
-        const int lin = tid + e * G::NT;
+      for (int e = 0; e < (kFBM * kFBK / 4) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
         const int r = lin >> 3, kq = (lin & 7) * 4;
         const int64_t rem = kdim - (k0 + kq);
         const int bytes = r < rows ? (rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0)) : 0;
@@ -337,8 +299,8 @@ struct RingLoader {
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < (G::BM * kFBK) / G::NT; ++e) {
-        const int lin = tid + e * G::NT;
+      for (int e = 0; e < (kFBM * kFBK) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
         const int r = lin >> 5, kk = lin & 31;
         const bool ok = r < rows && k0 + kk < kdim;
         cp_async4(sb + uint32_t(ring_a(r, kk) * 4), ok ? A + r * lda + k0 + kk : A, ok ? 4 : 0);
@@ -346,20 +308,20 @@ struct RingLoader {
     }
     if (b_vec) {
 #pragma unroll
-      for (int e = 0; e < (kFBK * kFBN / 4) / G::NT; ++e) {
-        const int lin = tid + e * G::NT;
+      for (int e = 0; e < (kFBK * kFBN / 4) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
         const int kk = lin >> 5, c = (lin & 31) * 4;
         const int64_t rem = cols - c;
         const int bytes = k0 + kk < kdim ? (rem >= 4 ? 16 : (rem > 0 ? int(rem) * 4 : 0)) : 0;
-        cp_async16(sb + uint32_t(ring_b<G::RAFloats>(kk, c) * 4), bytes ? B + (k0 + kk) * ldb + n0 + c : B, bytes);
+        cp_async16(sb + uint32_t(ring_b(kk, c) * 4), bytes ? B + (k0 + kk) * ldb + n0 + c : B, bytes);
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < (kFBK * kFBN) / G::NT; ++e) {
-        const int lin = tid + e * G::NT;
+      for (int e = 0; e < (kFBK * kFBN) / kFThreads; ++e) {
+        const int lin = tid + e * kFThreads;
         const int kk = lin >> 7, c = lin & 127;
         const bool ok = k0 + kk < kdim && c < cols;
-        cp_async4(sb + uint32_t(ring_b<G::RAFloats>(kk, c) * 4), ok ? B + (k0 + kk) * ldb + n0 + c : B, ok ? 4 : 0);
+        cp_async4(sb + uint32_t(ring_b(kk, c) * 4), ok ? B + (k0 + kk) * ldb + n0 + c : B, ok ? 4 : 0);
       }
     }
   }
@@ -367,11 +329,11 @@ struct RingLoader {
 
 // Semiring zero into the A columns k >= K of the last (partial) k-tile, so
 // padded k-pairs never produce a winning product.
-template <int S, class G = Geo128>
+template <int S>
 __device__ __forceinline__ void fix_k_tail(float* stage, int kvalid, int tid) {
   float* As = stage;
   const int width = kFBK - kvalid;
-  for (int i = tid; i < G::BM * width; i += G::NT) {
+  for (int i = tid; i < kFBM * width; i += kFThreads) {
     int row = i / width, kk = kvalid + i % width;
     As[row * kFApitch + kk] = FastOps<S>::zero();
   }
@@ -452,13 +414,11 @@ constexpr int kPanelMaxK = 256;
 constexpr size_t kFSmemPanel = size_t(kFStages) * kFAStage * 4 + size_t(kPanelMaxK) * kFBN * 4;
 static_assert(kFSmemPanel <= 232448, "B-panel kernel exceeds shared memory");
 
-template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true, bool BPANEL = false, int BMT = 128>
-__global__ void __launch_bounds__(2 * BMT, BMT == 64 ? 2 : 1)
+template <int S, bool ARGMAX, bool OUTI = false, bool PAIR = false, bool AVEC = true, bool BPANEL = false>
+__global__ void __launch_bounds__(kFThreads, 1)
 fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b, int use_tma) {
   using Op = FastOps<S>;
-  using G = FGeo<BMT, 2 * BMT>;
-  static_assert(!(BPANEL && BMT != 128), "the B panel runs with the default geometry");
   using CT = typename std::conditional<OUTI, int32_t, float>::type;
   if (gated_off(p)) return;
   extern __shared__ __align__(16) float smem[];
@@ -473,15 +433,15 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
   const float* __restrict__ B = static_cast<const float*>(p.b) + batch * p.sb;
   CT* __restrict__ C = static_cast<CT*>(p.c) + batch * p.sc;
   int32_t* __restrict__ IDX = ARGMAX ? p.argmax + batch * p.sc : nullptr;
-  const int64_t m0 = int64_t(blockIdx.x) * G::BM;
+  const int64_t m0 = int64_t(blockIdx.x) * kFBM;
   const int64_t n0 = int64_t(blockIdx.y) * kFBN;
   const int64_t ktiles = (p.k + kFBK - 1) / kFBK;
   const int kvalid_last = int(p.k - (ktiles - 1) * kFBK);
 
-  const TileLoader<G> ldr(A, B, p, m0, n0, tid, smem, AVEC);
-  uint16_t* cid = reinterpret_cast<uint16_t*>(sbytes + G::OffCid);
+  const TileLoader ldr(A, B, p, m0, n0, tid, smem, AVEC);
+  uint16_t* cid = reinterpret_cast<uint16_t*>(sbytes + kOffCid);
   if (ARGMAX && !PAIR) {
-    for (int i = tid; i < G::BM * kFBN; i += G::NT) cid[i] = kNoChunk;
+    for (int i = tid; i < kFBM * kFBN; i += kFThreads) cid[i] = kNoChunk;
   }
 
   float acc[8][8];
@@ -506,8 +466,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
   // stage layout: [A | B] per stage, or (BPANEL) three A stages then the B panel
   auto load_tile = [&](int stg, int64_t kt) {
     if constexpr (BPANEL) {
-      ldr.load_a_at(uint32_t(stg) * uint32_t(G::AStage * 4), kt);
-      ldr.load_b(uint32_t((kFStages - 1) * G::AStage + int(kt) * kFBStage) * 4u, kt);
+      ldr.load_a_at(uint32_t(stg) * uint32_t(kFAStage * 4), kt);
+      ldr.load_b(uint32_t((kFStages - 1) * kFAStage + int(kt) * kFBStage) * 4u, kt);
     } else {
       ldr.load(stg, kt);
     }
@@ -520,10 +480,10 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
   for (int64_t t = 0; t < ktiles; ++t) {
     cp_async_wait<kFStages - 2>();
     __syncthreads();
-    float* stage = smem + (t % kFStages) * (BPANEL ? G::AStage : G::StageFloats);
-    const float* bstage = BPANEL ? smem + kFStages * G::AStage + t * kFBStage : stage + G::AStage;
+    float* stage = smem + (t % kFStages) * (BPANEL ? kFAStage : kFStageFloats);
+    const float* bstage = BPANEL ? smem + kFStages * kFAStage + t * kFBStage : stage + kFAStage;
     if (t == ktiles - 1 && kvalid_last < kFBK) {
-      fix_k_tail<S, G>(stage, kvalid_last, tid);
+      fix_k_tail<S>(stage, kvalid_last, tid);
       __syncthreads();
     }
     {
@@ -573,7 +533,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
           float b0, b1 = 0.f;
           if constexpr (BPANEL) {   // k-pair of column lc in the resident panel ([k/2][n][2])
             const float2 bb = *reinterpret_cast<const float2*>(
-                smem + kFStages * G::AStage + (kg >> 1) * (kFBN * 2) + (wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)) * 2);
+                smem + kFStages * kFAStage + (kg >> 1) * (kFBN * 2) + (wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)) * 2);
             b0 = bb.x;
             b1 = bb.y;
           } else {
@@ -603,14 +563,14 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
 
   // -------------------------------------------- argmax: bucket by chunk
   __syncthreads();
-  uint16_t* list = reinterpret_cast<uint16_t*>(sbytes + G::OffList);
-  uint16_t* off = reinterpret_cast<uint16_t*>(sbytes + G::OffOff);
+  uint16_t* list = reinterpret_cast<uint16_t*>(sbytes + kOffList);
+  uint16_t* off = reinterpret_cast<uint16_t*>(sbytes + kOffOff);
   int* cnt = reinterpret_cast<int*>(smem);            // the stages are idle after the k loop
   int* cursor = cnt + (kFMaxChunks + 1);
   const int nchunks = int((ktiles + tiles_per_chunk - 1) / tiles_per_chunk);
-  for (int i = tid; i <= nchunks; i += G::NT) cnt[i] = 0;
+  for (int i = tid; i <= nchunks; i += kFThreads) cnt[i] = 0;
   __syncthreads();
-  for (int i = tid; i < G::BM * kFBN; i += G::NT) {
+  for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
     const uint16_t ch = cid[i];
     if (ch != kNoChunk) atomicAdd(&cnt[ch + 1], 1);
   }
@@ -630,12 +590,12 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
     }
   }
   __syncthreads();
-  for (int i = tid; i <= nchunks; i += G::NT) {
+  for (int i = tid; i <= nchunks; i += kFThreads) {
     off[i] = uint16_t(cnt[i]);
     if (i < nchunks) cursor[i] = cnt[i];
   }
   __syncthreads();
-  for (int i = tid; i < G::BM * kFBN; i += G::NT) {
+  for (int i = tid; i < kFBM * kFBN; i += kFThreads) {
     const uint16_t ch = cid[i];
     if (ch != kNoChunk) list[atomicAdd(&cursor[ch], 1)] = uint16_t(i);
   }
@@ -645,9 +605,9 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
   // Every output of chunk c had its last strict improvement in c, so its
   // final value is the max (min) of its products over c, and its reference
   // index is the first k of c whose product equals that value.  Tiles of the
-  // owned chunks stream through a G::RStages-deep ring (the chunk ids and the
+  // owned chunks stream through a kRStages-deep ring (the chunk ids and the
   // counters are dead now); a chunk is scanned once all its tiles have landed.
-  const RingLoader<G> rl(A, B, p, m0, n0, tid, smem, AVEC, b_vec != 0);
+  const RingLoader rl(A, B, p, m0, n0, tid, smem, AVEC, b_vec != 0);
   auto next_owned = [&](int c) {
     while (c < nchunks && off[c + 1] == off[c]) ++c;
     return c;
@@ -657,9 +617,9 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
   int64_t issued = 0;
   // TMA ring: slot base 1024-byte aligned for the 128-byte swizzle
   const bool tma = use_tma != 0 && (smem_u32(smem) & 1023) == 0;
-  const uint32_t bars = smem_u32(sbytes + G::OffBar);
+  const uint32_t bars = smem_u32(sbytes + kOffBar);
   if (tma && tid == 0) {
-    for (int s2 = 0; s2 < G::RStages; ++s2) mbar_init(bars + 8 * s2, 1);
+    for (int s2 = 0; s2 < kRStages; ++s2) mbar_init(bars + 8 * s2, 1);
     fence_proxy_async();
   }
   if (tma) __syncthreads();
@@ -668,17 +628,17 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
     while (ld_chunk < nchunks && issued < limit) {
       if (tma) {
         if (tid == 0) {
-          const int slot = int(issued % G::RStages);
-          const uint32_t sb = smem_u32(smem + slot * G::RStageFloats), bar = bars + 8 * slot;
-          mbar_expect_tx(bar, uint32_t(G::RStageFloats * 4));
+          const int slot = int(issued % kRStages);
+          const uint32_t sb = smem_u32(smem + slot * kRStageFloats), bar = bars + 8 * slot;
+          mbar_expect_tx(bar, uint32_t(kRStageFloats * 4));
           tma_load3(sb, &tma_a, int(ld_tile * kFBK), int(m0), int(batch), bar);
 #pragma unroll
           for (int j = 0; j < kFBN / 32; ++j)
-            tma_load3(sb + uint32_t((G::RAFloats + j * kFBK * 32) * 4), &tma_b, int(n0) + 32 * j, int(ld_tile * kFBK),
+            tma_load3(sb + uint32_t((kRAFloats + j * kFBK * 32) * 4), &tma_b, int(n0) + 32 * j, int(ld_tile * kFBK),
                       int(batch), bar);
         }
       } else {
-        rl.load(int(issued % G::RStages), ld_tile);
+        rl.load(int(issued % kRStages), ld_tile);
         cp_async_commit();
       }
       ++issued;
@@ -689,7 +649,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
       }
     }
   };
-  issue_until(G::RStages);
+  issue_until(kRStages);
   int64_t seq0 = 0;   // ring sequence number of the current chunk's first tile
   const int grp = tid >> 2, sub = tid & 3;
   for (int c = next_owned(0); c < nchunks; c = next_owned(c + 1)) {
@@ -703,7 +663,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
     bool landed = true;
     if (tma) {
       for (int64_t q = seq0; q < need; ++q)
-        landed = mbar_wait(bars + 8 * uint32_t(q % G::RStages), uint32_t((q / G::RStages) & 1)) && landed;
+        landed = mbar_wait(bars + 8 * uint32_t(q % kRStages), uint32_t((q / kRStages) & 1)) && landed;
     } else {
       const int64_t pending = issued - need;   // groups allowed to stay in flight
       if (pending >= 4) cp_async_wait<4>();
@@ -714,16 +674,16 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
     }
     __syncthreads();
     if (!__syncthreads_and(landed)) {   // a copy never arrived: mark the chunk's outputs, stop
-      for (int e = off[c] + tid; e < off[c + 1]; e += G::NT) {
+      for (int e = off[c] + tid; e < off[c + 1]; e += kFThreads) {
         const int o = list[e];
         IDX[(m0 + (o >> 7)) * p.ldc + (n0 + (o & 127))] = -2;
       }
       return;
     }
     // every thread is past the previous chunk: its ring slots may be refilled
-    issue_until(seq0 + G::RStages);
+    issue_until(seq0 + kRStages);
     const int beg = off[c], end = off[c + 1];
-    const int slot0 = int(seq0 % G::RStages);
+    const int slot0 = int(seq0 % kRStages);
     const int klast = int(i64min(kFBK, p.k - (t0 + nt - 1) * kFBK));   // valid k in the chunk's last tile
     // 64 groups of 4 lanes; lane `sub` owns k = sub, sub+4, ..., sub+28 of
     // every tile of the chunk.  Pass 1: group max of the products; pass 2:
@@ -735,20 +695,20 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
       // Full two-tile chunk: no k-range masks; pass 1 is a max3 tree, pass 2
       // a 16-bit equality mask whose lowest set bit is the lane's first
       // winning k (bit order = k order).
-      const float* st0 = smem + slot0 * G::RStageFloats;
-      const float* st1 = smem + (slot0 + 1 >= G::RStages ? slot0 + 1 - G::RStages : slot0 + 1) * G::RStageFloats;
-      for (int e0 = beg; e0 < end; e0 += 2 * (G::NT / 4)) {
+      const float* st0 = smem + slot0 * kRStageFloats;
+      const float* st1 = smem + (slot0 + 1 >= kRStages ? slot0 + 1 - kRStages : slot0 + 1) * kRStageFloats;
+      for (int e0 = beg; e0 < end; e0 += 2 * (kFThreads / 4)) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int e = e0 + u * (G::NT / 4) + grp;
+          const int e = e0 + u * (kFThreads / 4) + grp;
           const bool act = e < end;
           const int o = act ? list[e] : 0;
           const int lr = o >> 7, lc = o & 127;
           float pv[16];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            pv[i] = Op::mul(st0[ring_a(lr, sub + 4 * i)], st0[ring_b<G::RAFloats>(sub + 4 * i, lc)]);
-            pv[8 + i] = Op::mul(st1[ring_a(lr, sub + 4 * i)], st1[ring_b<G::RAFloats>(sub + 4 * i, lc)]);
+            pv[i] = Op::mul(st0[ring_a(lr, sub + 4 * i)], st0[ring_b(sub + 4 * i, lc)]);
+            pv[8 + i] = Op::mul(st1[ring_a(lr, sub + 4 * i)], st1[ring_b(sub + 4 * i, lc)]);
           }
           float m = Op::red3(Op::red3(Op::red3(pv[0], pv[1], pv[2]), Op::red3(pv[3], pv[4], pv[5]),
                                       Op::red3(pv[6], pv[7], pv[8])),
@@ -771,7 +731,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
           if (act && first != 0xFFFFFFFFu && kf == first) {
             const float* st = first >= unsigned(kFBK) ? st1 : st0;
             const int kk = int(first) & (kFBK - 1);
-            const float v = Op::mul(st[ring_a(lr, kk)], st[ring_b<G::RAFloats>(kk, lc)]);
+            const float v = Op::mul(st[ring_a(lr, kk)], st[ring_b(kk, lc)]);
             const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
             store_c(C, gofs, v);
             IDX[gofs] = int32_t(t0 * kFBK + first) + p.k_offset;
@@ -782,14 +742,14 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
       continue;
     }
     constexpr int kE = 2;
-    for (int e0 = beg; e0 < end; e0 += kE * (G::NT / 4)) {
+    for (int e0 = beg; e0 < end; e0 += kE * (kFThreads / 4)) {
       int o[kE];
       bool active[kE];
       float pr[kE][4][8];
       float best[kE];
 #pragma unroll
       for (int u = 0; u < kE; ++u) {
-        const int e = e0 + u * (G::NT / 4) + grp;
+        const int e = e0 + u * (kFThreads / 4) + grp;
         active[u] = e < end;
         o[u] = active[u] ? list[e] : 0;
         best[u] = Op::zero();
@@ -797,15 +757,15 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (j < nt) {
-          const int slot = slot0 + j >= G::RStages ? slot0 + j - G::RStages : slot0 + j;
-          const float* st = smem + slot * G::RStageFloats;
+          const int slot = slot0 + j >= kRStages ? slot0 + j - kRStages : slot0 + j;
+          const float* st = smem + slot * kRStageFloats;
           const int kc = j == nt - 1 ? klast : kFBK;
 #pragma unroll
           for (int u = 0; u < kE; ++u) {
             const int lr = o[u] >> 7, lc = o[u] & 127;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              pr[u][j][i] = Op::mul(st[ring_a(lr, sub + 4 * i)], st[ring_b<G::RAFloats>(sub + 4 * i, lc)]);
+              pr[u][j][i] = Op::mul(st[ring_a(lr, sub + 4 * i)], st[ring_b(sub + 4 * i, lc)]);
               if (sub + 4 * i < kc && Op::better(pr[u][j][i], best[u])) best[u] = pr[u][j][i];
             }
           }
