@@ -263,7 +263,9 @@ PIPE_VARIANTS = ("pair_fadd2_fmnmx3", "fadd2_alone", "fmnmx3_alone", "fadd_alone
                  "fadd_x2_fmnmx3", "fadd2_fmnmx_x2", "fadd_fmnmx", "engine_ktile_body",
                  "engine_ktile_body_with_barrier", "ktile_body_bpair_outer", "ktile_body_two_kpairs",
                  "ktile_body_two_kpairs_tree", "ktile_body_kquad_swapped", "ktile_body_kquad_aligned",
-                 "pair_b_lds128", "pair_b_lds64", "pair_b_lds128_prefetched")
+                 "pair_b_lds128", "pair_b_lds64", "pair_b_lds128_prefetched",
+                 "f64_dadd_alone", "f64_fmax_alone", "f64_dadd_fmax", "f64_dadd_strict_select",
+                 "f64_dadd_select_with_index")
 
 
 def pipe_rates(blocks_per_sm=(1, 2), iters=20000, variants=PIPE_VARIANTS):

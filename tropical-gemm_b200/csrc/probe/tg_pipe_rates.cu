@@ -176,6 +176,75 @@ __global__ void __launch_bounds__(256) pipe_kernel(int iters, long long* stamps,
   }
 }
 
+// Variants 18-22: f64 forms (32 accumulators of 4 rows x 8 columns per
+// thread, operands in registers; a product is one f64 add folded into its
+// accumulator):
+//  18 DADD alone; 19 fmax alone; 20 DADD + fmax (the reference's value-only
+//  form); 21 DADD + strict compare-and-select (the engine's f64 fold);
+//  22 DADD + compare + value and index selects (the argmax form).
+template <int V>
+__global__ void __launch_bounds__(256) pipe64_kernel(int iters, long long* stamps, float* sink) {
+  double acc[4][8];
+  int idx[4][8];
+  double a[4], b[8];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    a[r] = -1e-3 * double(r + 1) + 1e-6 * threadIdx.x;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      acc[r][c] = 0.25 * double(r * 8 + c);
+      idx[r][c] = 0;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) b[c] = -2e-3 * double(c + 1);
+  __syncthreads();
+  long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const double ar = V == 18 || V == 19 ? 0.0 : acc[r][0] + a[r];   // keeps the chain loop-carried
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        double& x = acc[r][c];
+        if (V == 18) {
+          x = x + b[c];
+        } else if (V == 19) {
+          x = fmax(x, b[c] + ar);
+        } else {
+          const double pr = ar + b[c];
+          if (V == 20) x = fmax(x, pr);
+          else if (V == 21) x = pr > x ? pr : x;
+          else {
+            const bool w = pr > x;
+            x = w ? pr : x;
+            idx[r][c] = w ? it : idx[r][c];
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  long long t1 = clock64();
+  double sum = 0.0;
+  int si = 0;
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      sum += acc[r][c];
+      si += idx[r][c];
+    }
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = float(sum) + float(si);
+  if (threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    stamps[3 * blockIdx.x] = smid;
+    stamps[3 * blockIdx.x + 1] = t0;
+    stamps[3 * blockIdx.x + 2] = t1;
+  }
+}
+
 // Variants 8 and 9: the engine's own k-tile body (tg::tile_math, MaxPlus,
 // values only) over one shared-memory stage that never changes; 9 adds the
 // k loop's barrier per k-tile.  Products per iteration: 64 outputs x 32 k.
@@ -332,14 +401,16 @@ __global__ void __launch_bounds__(256, 1) alt_kernel(int iters, long long* stamp
   }
 }
 
-constexpr int kVariants = 18;
+constexpr int kVariants = 23;
 constexpr int kProducts[kVariants] = {128, 128, 128, 64, 64, 128, 128, 64, 64 * tg::kFBK, 64 * tg::kFBK,
                                       64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK, 64 * tg::kFBK,
-                                      128, 128, 128};
+                                      128, 128, 128, 32, 32, 32, 32, 32};
 
 template <int V>
 cudaError_t launch(int blocks, int threads, int iters, long long* st, float* sink) {
-  if constexpr (V >= 15) {
+  if constexpr (V >= 18) {
+    pipe64_kernel<V><<<blocks, threads>>>(iters, st, sink);
+  } else if constexpr (V >= 15) {
     pipe_kernel<V><<<blocks, threads>>>(iters, st, sink);
   } else if constexpr (V >= 10) {
     alt_kernel<V><<<blocks, threads, tg::kFStageFloats * 4>>>(iters, st, sink);
@@ -376,7 +447,8 @@ extern "C" int tg_probe_pipe_rate(int variant, int blocks_per_sm, int threads, i
     const L table[kVariants] = {launch<0>, launch<1>, launch<2>, launch<3>, launch<4>,
                                 launch<5>, launch<6>, launch<7>, launch<8>, launch<9>,
                                 launch<10>, launch<11>, launch<12>, launch<13>, launch<14>,
-                                launch<15>, launch<16>, launch<17>};
+                                launch<15>, launch<16>, launch<17>, launch<18>, launch<19>,
+                                launch<20>, launch<21>, launch<22>};
     if (variant < 0 || variant >= kVariants) variant = 0;
     const L fn = table[variant];
     e = fn(blocks, threads, 8, st, sink);   // warm-up
