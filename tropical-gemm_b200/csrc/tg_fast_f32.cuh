@@ -339,6 +339,30 @@ __device__ __forceinline__ void fix_k_tail(float* stage, int kvalid, int tid) {
   }
 }
 
+// The 16 products a scan lane owns in a full two-tile chunk: k = sub + 4i
+// of each tile (i = 0..7), for output (lr, lc) of the ring slots st0, st1.
+// The swizzled positions (ring_a / ring_b) are taken apart once per output:
+// A's 16-byte group index is i ^ (lr & 7), and B's XOR key k & 7 is sub or
+// sub + 4 by the parity of i, so each load is a base plus an immediate.
+template <int S>
+__device__ __forceinline__ void chunk_products(const float* st0, const float* st1, int lr, int lc, int sub,
+                                               float (&pv)[16]) {
+  using Op = FastOps<S>;
+  const int ax = lr & 7, abase = lr * kFBK + sub;
+  int aoff[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) aoff[i] = abase + ((i ^ ax) << 2);
+  const int yb = (lc >> 2) & 7;
+  const int bbase = kRAFloats + (lc >> 5) * (kFBK * 32) + sub * 32 + (lc & 3);
+  const int b_even = bbase + ((yb ^ sub) << 2), b_odd = bbase + ((yb ^ (sub + 4)) << 2);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int bo = ((i & 1) ? b_odd : b_even) + 128 * i;
+    pv[i] = Op::mul(st0[aoff[i]], st0[bo]);
+    pv[8 + i] = Op::mul(st1[aoff[i]], st1[bo]);
+  }
+}
+
 // OUTI: C is int32 (the i32 path computes exactly in f32 on converted
 // operands and converts the result back).  acc_init: accumulator start value
 // (the semiring zero for f32; the reference's integer sentinel for i32 --
@@ -652,9 +676,90 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
   issue_until(kRStages);
   int64_t seq0 = 0;   // ring sequence number of the current chunk's first tile
   const int grp = tid >> 2, sub = tid & 3;
+  // a full chunk = two k-tiles with every k < K
+  auto full_chunk = [&](int cc) {
+    const int64_t tt = int64_t(cc) * tiles_per_chunk;
+    return tiles_per_chunk == 2 && tt + 2 <= ktiles && (tt + 2) * kFBK <= p.k;
+  };
   for (int c = next_owned(0); c < nchunks; c = next_owned(c + 1)) {
     const int64_t t0 = int64_t(c) * tiles_per_chunk;
     const int nt = int(i64min(tiles_per_chunk, ktiles - t0));
+    {
+      // Two full owned chunks resident in the ring at once (4 of its 6
+      // slots): scanned in one round with four entries per lane group, one
+      // barrier for both -- the scan is latency-bound per round, not
+      // throughput-bound.
+      const int c2 = next_owned(c + 1);
+      if (c2 < nchunks && full_chunk(c) && full_chunk(c2) && issued >= seq0 + 4) {
+        const int64_t need2 = seq0 + 4;
+        bool landed = true;
+        if (tma) {
+          for (int64_t q = seq0; q < need2; ++q)
+            landed = mbar_wait(bars + 8 * uint32_t(q % kRStages), uint32_t((q / kRStages) & 1)) && landed;
+        } else {
+          const int64_t pending = issued - need2;
+          if (pending >= 2) cp_async_wait<2>();
+          else if (pending == 1) cp_async_wait<1>();
+          else cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (!__syncthreads_and(landed)) {   // a copy never arrived: mark both chunks' outputs, stop
+          for (int e = off[c] + tid; e < off[c2 + 1]; e += kFThreads) {
+            const int o = list[e];
+            IDX[(m0 + (o >> 7)) * p.ldc + (n0 + (o & 127))] = -2;
+          }
+          return;
+        }
+        issue_until(seq0 + kRStages);
+        const int beg = off[c], mid = off[c + 1], end = off[c2 + 1];
+        const int64_t t0b = int64_t(c2) * tiles_per_chunk;
+        constexpr int kE4 = 4;
+        for (int e0 = beg; e0 < end; e0 += kE4 * (kFThreads / 4)) {
+#pragma unroll
+          for (int u = 0; u < kE4; ++u) {
+            const int e = e0 + u * (kFThreads / 4) + grp;
+            const bool act = e < end;
+            const bool second = e >= mid;
+            const int o = act ? list[e] : 0;
+            const int lr = o >> 7, lc = o & 127;
+            const int s0 = int((seq0 + (second ? 2 : 0)) % kRStages);
+            const float* st0 = smem + s0 * kRStageFloats;
+            const float* st1 = smem + (s0 + 1 >= kRStages ? s0 + 1 - kRStages : s0 + 1) * kRStageFloats;
+            float pv[16];
+            chunk_products<S>(st0, st1, lr, lc, sub, pv);
+            float m = Op::red3(Op::red3(Op::red3(pv[0], pv[1], pv[2]), Op::red3(pv[3], pv[4], pv[5]),
+                                        Op::red3(pv[6], pv[7], pv[8])),
+                               Op::red3(Op::red3(pv[9], pv[10], pv[11]), Op::red3(pv[12], pv[13], pv[14]), pv[15]),
+                               pv[15]);
+            float x = __shfl_xor_sync(0xffffffffu, m, 1);
+            m = Op::red3(m, x, x);
+            x = __shfl_xor_sync(0xffffffffu, m, 2);
+            m = Op::red3(m, x, x);
+            unsigned mask = 0;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) mask |= (pv[q] == m) ? (1u << q) : 0u;
+            unsigned kf = 0xFFFFFFFFu;
+            if (mask) {
+              const int q = __ffs(mask) - 1;
+              kf = unsigned(32 * (q >> 3) + sub + 4 * (q & 7));
+            }
+            unsigned first = min(kf, __shfl_xor_sync(0xffffffffu, kf, 1));
+            first = min(first, __shfl_xor_sync(0xffffffffu, first, 2));
+            if (act && first != 0xFFFFFFFFu && kf == first) {
+              const float* st = first >= unsigned(kFBK) ? st1 : st0;
+              const int kk = int(first) & (kFBK - 1);
+              const float v = Op::mul(st[ring_a(lr, kk)], st[ring_b(kk, lc)]);
+              const int64_t gofs = (m0 + lr) * p.ldc + (n0 + lc);
+              store_c(C, gofs, v);
+              IDX[gofs] = int32_t((second ? t0b : t0) * kFBK + first) + p.k_offset;
+            }
+          }
+        }
+        seq0 = need2;
+        c = c2;
+        continue;
+      }
+    }
     const int64_t need = seq0 + nt;
     if (issued < need) {   // chunks longer than two tiles: make room, then issue the rest
       __syncthreads();
@@ -705,11 +810,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
           const int o = act ? list[e] : 0;
           const int lr = o >> 7, lc = o & 127;
           float pv[16];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            pv[i] = Op::mul(st0[ring_a(lr, sub + 4 * i)], st0[ring_b(sub + 4 * i, lc)]);
-            pv[8 + i] = Op::mul(st1[ring_a(lr, sub + 4 * i)], st1[ring_b(sub + 4 * i, lc)]);
-          }
+          chunk_products<S>(st0, st1, lr, lc, sub, pv);
           float m = Op::red3(Op::red3(Op::red3(pv[0], pv[1], pv[2]), Op::red3(pv[3], pv[4], pv[5]),
                                       Op::red3(pv[6], pv[7], pv[8])),
                              Op::red3(Op::red3(pv[9], pv[10], pv[11]), Op::red3(pv[12], pv[13], pv[14]), pv[15]),
