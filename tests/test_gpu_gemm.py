@@ -381,3 +381,18 @@ def test_accumulate_rejects_other_dtypes():
     c = torch.zeros((4, 4), dtype=torch.float64, device=dev())
     with pytest.raises(ValueError):
         N.gemm_accumulate("maxplus", a, a, c, None, 0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("k", [1, 3, 4, 5, 130, 199, 256])
+def test_short_k_group_tracking_ties(semi, k):
+    """K <= 256 runs the resident-B-panel kernel that tracks the argmax per
+    4-k group: small integers make ties inside a group and across groups
+    frequent, and K not a multiple of 4 leaves a partial last group."""
+    rng = np.random.default_rng(k)
+    a = rng.integers(0 if semi == "maxmul" else -3, 4, (300, k)).astype(np.float32)
+    b = rng.integers(0 if semi == "maxmul" else -3, 4, (k, 260)).astype(np.float32)
+    c, am = engine(semi, a, b)
+    c0, am0 = oracle(semi, a, b)
+    assert same_bits(c, c0)
+    assert np.array_equal(am, am0)

@@ -423,6 +423,49 @@ __device__ __forceinline__ void tile_math(const float* a_stage, const float* b_s
   }
 }
 
+// Argmax tracked per 4-k group (the B-panel kernel, K <= 256): both k-pairs
+// of a group are folded into an output back to back (FADD2, FMNMX3, FADD2,
+// FMNMX3), then one strict compare against the value before the group
+// records the group of the last strict improvement -- 6 instructions per 4
+// products instead of the k-pair tracking's 8.  The epilogue resolves the
+// winning k inside that group from A (global) and the resident B panel.
+template <int S>
+__device__ __forceinline__ void tile_math_g4(const float* a_stage, const float* b_stage, int wm, int wn, int lm,
+                                             int ln, float (&acc)[8][8], int32_t (&pidx)[8][8], int64_t kbase) {
+  using Op = FastOps<S>;
+  const float* Ap = a_stage + (wm * 32 + lm) * kFApitch;
+  const float* Bp = b_stage + (wn * 64 + 2 * ln) * 2;
+#pragma unroll
+  for (int k4 = 0; k4 < kFBK; k4 += 4) {
+    float4 a[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) a[r] = *reinterpret_cast<const float4*>(Ap + r * 4 * kFApitch + k4);
+    float4 b0[4], b1[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      b0[q] = *reinterpret_cast<const float4*>(Bp + (k4 / 2) * (kFBN * 2) + q * 32);
+      b1[q] = *reinterpret_cast<const float4*>(Bp + (k4 / 2 + 1) * (kFBN * 2) + q * 32);
+    }
+    const int32_t kg = int32_t(kbase + k4);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float l0, h0, l1, h1;
+          Op::pair(l0, h0, a[r].x, a[r].y, e ? b0[q].z : b0[q].x, e ? b0[q].w : b0[q].y);
+          Op::pair(l1, h1, a[r].z, a[r].w, e ? b1[q].z : b1[q].x, e ? b1[q].w : b1[q].y);
+          float& av = acc[r][2 * q + e];
+          const float nv = Op::red3(Op::red3(av, l0, h0), l1, h1);
+          if (Op::better(nv, av)) pidx[r][2 * q + e] = kg;
+          av = nv;
+        }
+      }
+    }
+  }
+}
+
 // PAIR (with ARGMAX, for short K): instead of chunk detection + re-stream,
 // track the winner per k-pair in registers -- after each FADD2/FMNMX3 step a
 // strict compare of the new running value against the old one, and on an
@@ -432,8 +475,8 @@ __device__ __forceinline__ void tile_math(const float* a_stage, const float* b_s
 // AVEC: A rows are 16-byte aligned (else A is staged by 4-byte copies).
 // BPANEL (PAIR, K <= kPanelMaxK): B's whole 128-column panel stays resident
 // in shared memory (each k-tile's B lands in its own panel slice, A alone
-// cycles through the stages), so the epilogue reloads the winning k-pair of
-// B from shared memory instead of scattered global reads.
+// cycles through the stages); the argmax is tracked per 4-k group
+// (tile_math_g4) and the epilogue resolves it from A (global) and the panel.
 constexpr int kPanelMaxK = 256;
 constexpr size_t kFSmemPanel = size_t(kFStages) * kFAStage * 4 + size_t(kPanelMaxK) * kFBN * 4;
 static_assert(kFSmemPanel <= 232448, "B-panel kernel exceeds shared memory");
@@ -515,7 +558,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
       if (nt < ktiles) load_tile(int(nt % kFStages), nt);
       cp_async_commit();
     }
-    tile_math<S, PAIR>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    if constexpr (BPANEL) tile_math_g4<S>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    else tile_math<S, PAIR>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
     if (ARGMAX && !PAIR && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
       // chunk boundary: remember the chunk of each output's latest strict improvement
       const uint16_t chunk = uint16_t(t / tiles_per_chunk);
@@ -553,17 +597,29 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
         float v = acc_init;
         int32_t kw = 0;
         if (kg < 0 && p.accumulate) continue;   // nothing beat the previous slices: keep C and argmax
-        if (kg >= 0) {
-          float b0, b1 = 0.f;
-          if constexpr (BPANEL) {   // k-pair of column lc in the resident panel ([k/2][n][2])
-            const float2 bb = *reinterpret_cast<const float2*>(
-                smem + kFStages * kFAStage + (kg >> 1) * (kFBN * 2) + (wn * 64 + 16 * (c >> 1) + 2 * ln + (c & 1)) * 2);
-            b0 = bb.x;
-            b1 = bb.y;
-          } else {
-            b0 = B[int64_t(kg) * p.ldb + gc];
-            if (kg + 1 < p.k) b1 = B[int64_t(kg + 1) * p.ldb + gc];
+        if (kg >= 0 && BPANEL) {
+          // kg: first k of the 4-k group of the last strict improvement; the
+          // winner is the group's first k whose product equals the final value
+          const float* pan = smem + kFStages * kFAStage + (kg >> 1) * (kFBN * 2) + lc * 2;
+          const float2 bb0 = *reinterpret_cast<const float2*>(pan);
+          const float2 bb1 = *reinterpret_cast<const float2*>(pan + kFBN * 2);
+          const float bv[4] = {bb0.x, bb0.y, bb1.x, bb1.y};
+          const float* ar = A + gr * p.lda + kg;
+          v = acc[r][c];
+          kw = kg;
+#pragma unroll
+          for (int i = 3; i >= 0; --i) {
+            if (kg + i < p.k) {
+              const float pr = Op::mul(ar[i], bv[i]);
+              if (pr == acc[r][c]) {
+                v = pr;
+                kw = kg + i;
+              }
+            }
           }
+        } else if (kg >= 0) {
+          const float b0 = B[int64_t(kg) * p.ldb + gc];
+          const float b1 = kg + 1 < p.k ? B[int64_t(kg + 1) * p.ldb + gc] : 0.f;
           const float lo = Op::mul(A[gr * p.lda + kg], b0);
           if (lo == acc[r][c] || kg + 1 >= p.k) {
             v = lo;
