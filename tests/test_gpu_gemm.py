@@ -206,7 +206,7 @@ def test_large_square_vs_oracle_sampled_rows():
 
 @pytest.mark.parametrize("semi", SEMIS)
 @pytest.mark.parametrize("pattern", ["increasing", "decreasing", "plateau"])
-@pytest.mark.parametrize("k", [900, 1500])
+@pytest.mark.parametrize("k", [200, 900, 1500])
 def test_argmax_improvement_patterns(semi, pattern, k):
     """Running values that improve in every k-chunk, only in the first one,
     or tie on a long plateau: the pair (K <= 1024) and chunk bookkeeping must
