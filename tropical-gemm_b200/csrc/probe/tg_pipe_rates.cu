@@ -255,7 +255,6 @@ __global__ void __launch_bounds__(256, 1) body_kernel(int iters, long long* stam
   __syncthreads();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float acc[8][8];
-  int32_t unused[1][1];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
@@ -263,7 +262,7 @@ __global__ void __launch_bounds__(256, 1) body_kernel(int iters, long long* stam
   long long t0 = clock64();
   for (int it = 0; it < iters; ++it) {
     if (V == 9) __syncthreads();
-    tg::tile_math<tg::kMaxPlus, false>(stage, stage + tg::kFAStage, warp >> 1, warp & 1, lane >> 3, lane & 7, acc, unused, 0);
+    tg::tile_math<tg::kMaxPlus>(stage, stage + tg::kFAStage, warp >> 1, warp & 1, lane >> 3, lane & 7, acc);
   }
   __syncthreads();
   long long t1 = clock64();

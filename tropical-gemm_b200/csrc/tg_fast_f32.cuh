@@ -25,9 +25,9 @@
 //    when nothing beats the semiring zero), and its exact bits (the sign of
 //    a zero included).
 //  * Short K (the host picks PAIR for K <= 1024, where the re-stream's fixed
-//    cost per output would dominate): the pair index of the last strict
-//    improvement is kept in registers and the winning k within that pair is
-//    settled in the epilogue from the two products reloaded from A and B.
+//    cost per output would dominate): the 4-k group of the last strict
+//    improvement is kept in registers and the winning k within that group is
+//    settled in the epilogue from the four products reloaded from A and B.
 #pragma once
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
@@ -373,13 +373,10 @@ __device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
 }
 
 // The k loop body over one staged k-tile: this thread's 8x8 outputs, rows
-// wm*32 + 4r + lm, columns wn*64 + 16(c>>1) + 2ln + (c&1).  PAIR also keeps,
-// per output, the first k of the k-pair that held the last strict
-// improvement (kbase = the tile's first k).
-template <int S, bool PAIR>
+// wm*32 + 4r + lm, columns wn*64 + 16(c>>1) + 2ln + (c&1).
+template <int S>
 __device__ __forceinline__ void tile_math(const float* a_stage, const float* b_stage, int wm, int wn, int lm, int ln,
-                                          float (&acc)[8][8], int32_t (&pidx)[PAIR ? 8 : 1][PAIR ? 8 : 1],
-                                          int64_t kbase) {
+                                          float (&acc)[8][8]) {
   using Op = FastOps<S>;
   const float* Ap = a_stage + (wm * 32 + lm) * kFApitch;
   const float* Bp = b_stage + (wn * 64 + 2 * ln) * 2;
@@ -401,34 +398,22 @@ __device__ __forceinline__ void tile_math(const float* a_stage, const float* b_s
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float lo, hi;
-          if (PAIR) {
-            const int32_t kg = int32_t(kbase + k4 + 2 * h);
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              Op::pair(lo, hi, a0, a1, e ? bq[q].z : bq[q].x, e ? bq[q].w : bq[q].y);
-              float& av = acc[r][2 * q + e];
-              const float nv = Op::red3(av, lo, hi);
-              if (Op::better(nv, av)) pidx[r][2 * q + e] = kg;
-              av = nv;
-            }
-          } else {
-            Op::pair(lo, hi, a0, a1, bq[q].x, bq[q].y);
-            acc[r][2 * q] = Op::red3(acc[r][2 * q], lo, hi);
-            Op::pair(lo, hi, a0, a1, bq[q].z, bq[q].w);
-            acc[r][2 * q + 1] = Op::red3(acc[r][2 * q + 1], lo, hi);
-          }
+          Op::pair(lo, hi, a0, a1, bq[q].x, bq[q].y);
+          acc[r][2 * q] = Op::red3(acc[r][2 * q], lo, hi);
+          Op::pair(lo, hi, a0, a1, bq[q].z, bq[q].w);
+          acc[r][2 * q + 1] = Op::red3(acc[r][2 * q + 1], lo, hi);
         }
       }
     }
   }
 }
 
-// Argmax tracked per 4-k group (the B-panel kernel, K <= 256): both k-pairs
+// Argmax tracked per 4-k group (short K): both k-pairs
 // of a group are folded into an output back to back (FADD2, FMNMX3, FADD2,
 // FMNMX3), then one strict compare against the value before the group
 // records the group of the last strict improvement -- 6 instructions per 4
-// products instead of the k-pair tracking's 8.  The epilogue resolves the
-// winning k inside that group from A (global) and the resident B panel.
+// products (values only: 4).  The epilogue resolves the winning k inside
+// that group from A (global) and B (the resident panel, or global).
 template <int S>
 __device__ __forceinline__ void tile_math_g4(const float* a_stage, const float* b_stage, int wm, int wn, int lm,
                                              int ln, float (&acc)[8][8], int32_t (&pidx)[8][8], int64_t kbase) {
@@ -467,16 +452,14 @@ __device__ __forceinline__ void tile_math_g4(const float* a_stage, const float* 
 }
 
 // PAIR (with ARGMAX, for short K): instead of chunk detection + re-stream,
-// track the winner per k-pair in registers -- after each FADD2/FMNMX3 step a
-// strict compare of the new running value against the old one, and on an
-// improvement the first of the two products that attains it (value bits and
-// index).  ~3 instructions per product instead of ~1, but no re-stream,
-// whose cost per output does not shrink with K.
+// track the winner per 4-k group in registers (tile_math_g4): 1.5
+// instructions per product instead of ~1, but no re-stream, whose cost per
+// output does not shrink with K.
 // AVEC: A rows are 16-byte aligned (else A is staged by 4-byte copies).
 // BPANEL (PAIR, K <= kPanelMaxK): B's whole 128-column panel stays resident
 // in shared memory (each k-tile's B lands in its own panel slice, A alone
-// cycles through the stages); the argmax is tracked per 4-k group
-// (tile_math_g4) and the epilogue resolves it from A (global) and the panel.
+// cycles through the stages), so the epilogue reads the winning group's B
+// values from shared memory instead of scattered global loads.
 constexpr int kPanelMaxK = 256;
 constexpr size_t kFSmemPanel = size_t(kFStages) * kFAStage * 4 + size_t(kPanelMaxK) * kFBN * 4;
 static_assert(kFSmemPanel <= 232448, "B-panel kernel exceeds shared memory");
@@ -558,8 +541,8 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
       if (nt < ktiles) load_tile(int(nt % kFStages), nt);
       cp_async_commit();
     }
-    if constexpr (BPANEL) tile_math_g4<S>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
-    else tile_math<S, PAIR>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    if constexpr (PAIR) tile_math_g4<S>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    else tile_math<S>(stage, bstage, wm, wn, lm, ln, acc);
     if (ARGMAX && !PAIR && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
       // chunk boundary: remember the chunk of each output's latest strict improvement
       const uint16_t chunk = uint16_t(t / tiles_per_chunk);
@@ -597,13 +580,19 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
         float v = acc_init;
         int32_t kw = 0;
         if (kg < 0 && p.accumulate) continue;   // nothing beat the previous slices: keep C and argmax
-        if (kg >= 0 && BPANEL) {
+        if (kg >= 0) {
           // kg: first k of the 4-k group of the last strict improvement; the
           // winner is the group's first k whose product equals the final value
-          const float* pan = smem + kFStages * kFAStage + (kg >> 1) * (kFBN * 2) + lc * 2;
-          const float2 bb0 = *reinterpret_cast<const float2*>(pan);
-          const float2 bb1 = *reinterpret_cast<const float2*>(pan + kFBN * 2);
-          const float bv[4] = {bb0.x, bb0.y, bb1.x, bb1.y};
+          float bv[4];
+          if constexpr (BPANEL) {   // two k-pairs of column lc in the resident panel ([k/2][n][2])
+            const float* pan = smem + kFStages * kFAStage + (kg >> 1) * (kFBN * 2) + lc * 2;
+            const float2 bb0 = *reinterpret_cast<const float2*>(pan);
+            const float2 bb1 = *reinterpret_cast<const float2*>(pan + kFBN * 2);
+            bv[0] = bb0.x; bv[1] = bb0.y; bv[2] = bb1.x; bv[3] = bb1.y;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) bv[i] = kg + i < p.k ? B[int64_t(kg + i) * p.ldb + gc] : 0.f;
+          }
           const float* ar = A + gr * p.lda + kg;
           v = acc[r][c];
           kw = kg;
@@ -616,17 +605,6 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
                 kw = kg + i;
               }
             }
-          }
-        } else if (kg >= 0) {
-          const float b0 = B[int64_t(kg) * p.ldb + gc];
-          const float b1 = kg + 1 < p.k ? B[int64_t(kg + 1) * p.ldb + gc] : 0.f;
-          const float lo = Op::mul(A[gr * p.lda + kg], b0);
-          if (lo == acc[r][c] || kg + 1 >= p.k) {
-            v = lo;
-            kw = kg;
-          } else {
-            v = Op::mul(A[gr * p.lda + kg + 1], b1);
-            kw = kg + 1;
           }
         }
         store_c(C, gr * p.ldc + gc, v);
