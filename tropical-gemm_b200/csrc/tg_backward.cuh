@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(256) hist_rows_warp_kernel(HistArgs p) {
 }
 
 // grad_out[k, c] (+)= sum_r [arg[r,c] == k] * gc[r,c] * (w ? w[r*ldw + k] : 1)
-// One CTA per 32-column strip; 256 threads = 8 row lanes x 32 columns, four
+// One CTA per 32-column strip; 256 threads = 8 row lanes x 32 columns, eight
 // rows per lane in flight.
 template <typename T>
 __global__ void __launch_bounds__(256) hist_cols_kernel(HistArgs p) {
@@ -118,16 +118,16 @@ __global__ void __launch_bounds__(256) hist_cols_kernel(HistArgs p) {
   const int64_t c = c0 + lane;
   if (c < p.cols) {
     int64_t r = rl;
-    for (; r + 24 < p.rows; r += 32) {
-      int32_t kk[4];
-      T g[4];
+    for (; r + 56 < p.rows; r += 64) {
+      int32_t kk[8];
+      T g[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         kk[u] = arg[(r + 8 * u) * p.ldc + c];
         g[u] = gc[(r + 8 * u) * p.ldc + c];
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         if (kk[u] < 0 || kk[u] >= p.k) continue;
         T v = g[u];
         if (w) v = v * w[(r + 8 * u) * p.ldw + kk[u]];
