@@ -79,7 +79,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 bool encode_tma_f32(const void* base, int64_t inner, int64_t rows, int64_t ld, int64_t batch, int64_t bstride,
-                    uint32_t box_inner, uint32_t box_rows, CUtensorMap* out) {
+                    uint32_t box_inner, uint32_t box_rows, CUtensorMap* out, bool swizzle) {
   static std::once_flag once;
   static EncodeTiledFn fn = nullptr;
   std::call_once(once, [] {
@@ -96,8 +96,17 @@ bool encode_tma_f32(const void* base, int64_t inner, int64_t rows, int64_t ld, i
   const cuuint32_t box[3] = {box_inner, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int kernel_regs(const void* kern) {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return fa.numRegs;
 }
 
 int sm_count() {

@@ -8,11 +8,13 @@
 #pragma once
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include "tg_internal.h"
 #include "tg_semiring.cuh"
 #include "tg_generic.cuh"
 #include "tg_fast_f32.cuh"
+#include "tg_argmax_fused.cuh"
 #include "tg_wide.cuh"
 
 namespace tgi {
@@ -31,6 +33,86 @@ __global__ void fill_zero_kernel(T* c, int32_t* idx, int64_t m, int64_t n, int64
 }
 
 constexpr int64_t kPairMaxK = 1024;
+
+// Long-K f32 argmax through the persistent fused-resolution kernel.  Needs
+// 16-byte aligned A and B rows (TMA / 16-byte copies), a fresh C (no
+// accumulate), K <= 2 x 1024 x 32 and stream-ordered scratch for two copies
+// of B; returns TG_ERR_UNSUPPORTED (nothing launched) when any of that is
+// missing, and the caller uses the chunk re-stream kernel instead.
+// By default it runs where it measured faster than the chunk kernel -- K >=
+// 4096 and at least 16 tiles per SM (8192^3: 42.0 vs 42.9 ms; 4096^3: 6.13
+// vs 5.89 ms) -- TROPICAL_GEMM_ARGMAX_FUSED=1 selects it wherever it is
+// supported and =0 never.
+template <int S>
+tg_status launch_argmax_fused(const Problem& P, cudaStream_t st, float acc_init) {
+  static const int mode = [] {
+    const char* e = std::getenv("TROPICAL_GEMM_ARGMAX_FUSED");
+    return e && e[0] == '0' ? 0 : (e && e[0] == '1' ? 1 : -1);
+  }();
+  const tg::GemmArgs& g = P.g;
+  if (mode == 0 || g.accumulate || g.gate) return TG_ERR_UNSUPPORTED;
+  const int64_t ntiles = P.batch * ((g.m + tg::kFBM - 1) / tg::kFBM) * ((g.n + tg::kFBN - 1) / tg::kFBN);
+  if (mode < 0 && (g.k < 4096 || ntiles < 16 * int64_t(sm_count()))) return TG_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(g.a) & 15) || (reinterpret_cast<uintptr_t>(g.b) & 15) || g.lda % 4 || g.ldb % 4 ||
+      (P.batch > 1 && (g.sa % 4 || g.sb % 4)))
+    return TG_ERR_UNSUPPORTED;
+  // chunks of two k-tiles, at most kFMaxChunks of them
+  if (P.batch > 65535 || g.n > (int64_t(1) << 30) || g.k > int64_t(2) * tg::kFMaxChunks * tg::kFBK)
+    return TG_ERR_UNSUPPORTED;
+  auto kern = tg::fast_f32_argmax_fused_kernel<S>;
+  if (ensure_smem(reinterpret_cast<const void*>(kern), tg::kFSmemFused) != TG_OK) {
+    clear_error();
+    return TG_ERR_UNSUPPORTED;
+  }
+  // scratch: B k-pair interleaved ([K2][np][2]) then B transposed ([N][kp])
+  const int64_t np = (g.n + 3) & ~int64_t(3), k2 = (g.k + 1) / 2, kp = (g.k + 3) & ~int64_t(3);
+  const size_t il_bytes = (size_t(P.batch) * size_t(k2) * size_t(np) * 8 + 1023) & ~size_t(1023);
+  const size_t bytes = il_bytes + size_t(P.batch) * size_t(g.n) * size_t(kp) * 4;
+  void* ws = nullptr;
+  if (scratch_alloc(&ws, bytes, st) != cudaSuccess) {
+    cudaGetLastError();
+    return TG_ERR_UNSUPPORTED;
+  }
+  float* bil = static_cast<float*>(ws);
+  float* bt = reinterpret_cast<float*>(static_cast<char*>(ws) + il_bytes);
+  CUtensorMap tm_bil, tm_bt;
+  std::memset(&tm_bil, 0, sizeof(tm_bil));
+  std::memset(&tm_bt, 0, sizeof(tm_bt));
+  if (!encode_tma_f32(bil, 2 * np, k2, 2 * np, P.batch, 2 * np * k2, 2 * tg::kFBN, tg::kFBK / 2, &tm_bil, false) ||
+      !encode_tma_f32(bt, g.k, g.n, kp, P.batch, g.n * kp, tg::kFBK, tg::kFBN, &tm_bt, true)) {
+    scratch_free(ws, st);
+    return TG_ERR_UNSUPPORTED;
+  }
+  {
+    const int64_t total = k2 * np;
+    const unsigned gx = unsigned(std::min<int64_t>((total + 255) / 256, 4 * int64_t(sm_count())));
+    tg::interleave_b_kernel<<<dim3(gx, unsigned(P.batch)), 256, 0, st>>>(static_cast<const float*>(g.b), g.k, g.n,
+                                                                         g.ldb, g.sb, bil, np);
+    tg_status s = check_launch("interleave_b_kernel launch");
+    if (s == TG_OK) {
+      const int64_t bx = (g.n + 31) / 32, by = std::min<int64_t>((kp + 31) / 32, 65535);
+      if (bx > 0x7fffffff) s = fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
+      else {
+        tg::transpose_b_kernel<<<dim3(unsigned(bx), unsigned(by), unsigned(P.batch)), 256, 0, st>>>(
+            static_cast<const float*>(g.b), g.k, g.n, g.ldb, g.sb, bt, kp);
+        s = check_launch("transpose_b_kernel launch");
+      }
+    }
+    if (s != TG_OK) {
+      scratch_free(ws, st);
+      return s;
+    }
+  }
+  tg::FusedArgs w;
+  w.p = g;
+  w.nbatch = P.batch;
+  w.acc_init = acc_init;
+  const unsigned grid = unsigned(std::min<int64_t>(ntiles, sm_count()));
+  kern<<<grid, tg::kFThreads, tg::kFSmemFused, st>>>(w, tm_bil, tm_bt);
+  tg_status s = check_launch("fast_f32_argmax_fused_kernel launch");
+  scratch_free(ws, st);
+  return s;
+}
 
 template <int S, bool ARGMAX, bool OUTI = false>
 tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
@@ -61,6 +143,12 @@ tg_status launch_fast_f32(const Problem& P, cudaStream_t st, float acc_init) {
   const int b_vec = ((reinterpret_cast<uintptr_t>(P.g.b) & 15) == 0 && P.g.ldb % 4 == 0 &&
                      (P.batch == 1 || P.g.sb % 4 == 0)) ? 1 : 0;
   while ((ktiles + tpc - 1) / tpc > tg::kFMaxChunks) tpc *= 2;
+  if constexpr (ARGMAX && !OUTI) {
+    if (!pair) {
+      const tg_status s = launch_argmax_fused<S>(P, st, acc_init);
+      if (s != TG_ERR_UNSUPPORTED) return s;
+    }
+  }
   // (Short K: the re-stream costs as much per output as at long K, so the
   // argmax is tracked per k-pair in registers instead; measured crossover K ~ 1024-1536.)
   const int64_t gx = (P.g.m + tg::kFBM - 1) / tg::kFBM;

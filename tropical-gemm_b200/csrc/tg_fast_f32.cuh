@@ -374,13 +374,13 @@ __device__ __forceinline__ void store_c(CT* C, int64_t o, float v) {
 
 // The k loop body over one staged k-tile: this thread's 8x8 outputs, rows
 // wm*32 + 4r + lm, columns wn*64 + 16(c>>1) + 2ln + (c&1).
-template <int S>
+template <int S, int KUNROLL = kFBK / 4>   // KUNROLL: 4-k steps unrolled per loop trip
 __device__ __forceinline__ void tile_math(const float* a_stage, const float* b_stage, int wm, int wn, int lm, int ln,
                                           float (&acc)[8][8]) {
   using Op = FastOps<S>;
   const float* Ap = a_stage + (wm * 32 + lm) * kFApitch;
   const float* Bp = b_stage + (wn * 64 + 2 * ln) * 2;
-#pragma unroll
+#pragma unroll KUNROLL
   for (int k4 = 0; k4 < kFBK; k4 += 4) {
     float4 a[8];
 #pragma unroll

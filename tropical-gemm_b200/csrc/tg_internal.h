@@ -34,11 +34,13 @@ void scratch_free(void* p, cudaStream_t st);
 bool fast_f32_ok(const Problem& P);
 
 // A 3-D f32 tensor map (inner, rows, batch) with a (box_inner x box_rows x 1)
-// box, 128-byte swizzle and zero fill out of bounds, for the TMA re-stream.
+// box, 128-byte swizzle (or none) and zero fill out of bounds, for TMA loads.
 // False when the driver entry point is missing or the layout is not
 // encodable (16-byte aligned base and strides are the caller's check).
 bool encode_tma_f32(const void* base, int64_t inner, int64_t rows, int64_t ld, int64_t batch, int64_t bstride,
-                    uint32_t box_inner, uint32_t box_rows, CUtensorMap* out);
+                    uint32_t box_inner, uint32_t box_rows, CUtensorMap* out, bool swizzle = true);
+// Registers per thread the kernel launches with (0 when unknown).
+int kernel_regs(const void* kern);
 
 // One semiring's dispatch over the four dtypes (canonical row-major problem).
 template <int S> tg_status dispatch(tg_dtype dtype, const Problem& P, cudaStream_t st);
