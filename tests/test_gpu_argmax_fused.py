@@ -23,10 +23,10 @@ def test_fused_kernel_forced_cases():
 
 
 def test_fused_kernel_default_selection_sampled_rows():
-    """8192 x 4096 x 8192 (K >= 4096, 32 tiles per SM): the default dispatch
-    takes the fused kernel; full rows of a sample against the oracle."""
+    """8192^3 (K >= 8192, 27.7 tiles per SM): the default dispatch takes the
+    fused kernel; full rows of a sample against the oracle."""
     rng = np.random.default_rng(7)
-    m, k, n = 8192, 4096, 8192
+    m, k, n = 8192, 8192, 8192
     a = rng.standard_normal((m, k), dtype=np.float32)
     b = rng.standard_normal((k, n), dtype=np.float32)
     c, am = engine("maxplus", a, b)

@@ -40,8 +40,9 @@ constexpr int64_t kPairMaxK = 1024;
 // of B; returns TG_ERR_UNSUPPORTED (nothing launched) when any of that is
 // missing, and the caller uses the chunk re-stream kernel instead.
 // By default it runs where it measured faster than the chunk kernel -- K >=
-// 4096 and at least 16 tiles per SM (8192^3: 42.0 vs 42.9 ms; 4096^3: 6.13
-// vs 5.89 ms) -- TROPICAL_GEMM_ARGMAX_FUSED=1 selects it wherever it is
+// 8192 and at least 16 tiles per SM (8192^3: 41.9 vs 42.9 ms; 8192 x 16384
+// x 8192: 78.1 vs 82.0; but 16384 x 4096 x 16384: 93.3 vs 92.7 and 4096^3:
+// 6.13 vs 5.89) -- TROPICAL_GEMM_ARGMAX_FUSED=1 selects it wherever it is
 // supported and =0 never.
 template <int S>
 tg_status launch_argmax_fused(const Problem& P, cudaStream_t st, float acc_init) {
@@ -52,7 +53,7 @@ tg_status launch_argmax_fused(const Problem& P, cudaStream_t st, float acc_init)
   const tg::GemmArgs& g = P.g;
   if (mode == 0 || g.accumulate || g.gate) return TG_ERR_UNSUPPORTED;
   const int64_t ntiles = P.batch * ((g.m + tg::kFBM - 1) / tg::kFBM) * ((g.n + tg::kFBN - 1) / tg::kFBN);
-  if (mode < 0 && (g.k < 4096 || ntiles < 16 * int64_t(sm_count()))) return TG_ERR_UNSUPPORTED;
+  if (mode < 0 && (g.k < 8192 || ntiles < 16 * int64_t(sm_count()))) return TG_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(g.a) & 15) || (reinterpret_cast<uintptr_t>(g.b) & 15) || g.lda % 4 || g.ldb % 4 ||
       (P.batch > 1 && (g.sa % 4 || g.sb % 4)))
     return TG_ERR_UNSUPPORTED;
