@@ -286,6 +286,103 @@ int tg_oracle_simd_maxplus_f32(int64_t m, int64_t n, int64_t k, const float* a, 
 }
 
 /*
+ * SIMD argmax path for f32, all three semirings (the "AVX-512/AVX2 CPU path
+ * for argmax" the reference lacks: its argmax microkernel,
+ * crates/tropical-gemm/src/core/kernel.rs:119-167, is scalar).  Same BLIS
+ * blocking as the AVX2 value-only path above (mc=nc=256, kc=512, 8x8 tiles),
+ * one 8-lane accumulator and one 8-lane index vector per row of C.  Per k
+ * (ascending, global k = pc + p) the product vector is compared strictly
+ * against the accumulator (ordered compare: NaN never wins) and both the
+ * value and the index are blended under that mask -- lane for lane the
+ * scalar rule of types/max_plus.rs:67-73 (keep the earlier k on ties), so
+ * values and indices equal tg_oracle_blis_argmax_f32 bit for bit.
+ * Returns 1 when the build has no AVX2.
+ */
+int tg_oracle_simd_argmax_f32(int semiring, int64_t m, int64_t n, int64_t k, const float* a, const float* b,
+                              float* c, int32_t* argmax, int nthreads) {
+#if defined(__AVX2__)
+  if (nthreads < 1) nthreads = 1;
+  const float z = zero_f32(semiring);
+  for (int64_t e = 0; e < m * n; ++e) { c[e] = z; argmax[e] = 0; }
+  if (m == 0 || n == 0 || k == 0) return 0;
+  const int64_t njc = (n + SNC - 1) / SNC;
+  const int minplus = semiring == MINPLUS, maxmul = semiring == MAXMUL;
+  _Pragma("omp parallel num_threads(nthreads)")
+  {
+    float* pa = (float*)aligned_alloc(32, sizeof(float) * SMC * SKC);
+    float* pb = (float*)aligned_alloc(32, sizeof(float) * SKC * SNC);
+    _Pragma("omp for schedule(dynamic, 1)")
+    for (int64_t jb = 0; jb < njc; ++jb) {
+      const int64_t jc = jb * SNC, nc = (n - jc) < SNC ? (n - jc) : SNC;
+      for (int64_t pc = 0; pc < k; pc += SKC) {
+        const int64_t kc = (k - pc) < SKC ? (k - pc) : SKC;
+        for (int64_t jr = 0; jr < nc; jr += SNR)
+          for (int64_t p = 0; p < kc; ++p)
+            for (int j = 0; j < SNR; ++j)
+              pb[jr * kc + p * SNR + j] = (jr + j < nc) ? b[(pc + p) * n + jc + jr + j] : 0.0f;
+        for (int64_t ic = 0; ic < m; ic += SMC) {
+          const int64_t mc = (m - ic) < SMC ? (m - ic) : SMC;
+          for (int64_t ir = 0; ir < mc; ir += SMR)
+            for (int64_t p = 0; p < kc; ++p)
+              for (int i = 0; i < SMR; ++i)
+                pa[ir * kc + p * SMR + i] = (ir + i < mc) ? a[(ic + ir + i) * k + pc + p] : 0.0f;
+          for (int64_t jr = 0; jr < nc; jr += SNR) {
+            const int nr = (nc - jr) < SNR ? (int)(nc - jr) : SNR;
+            for (int64_t ir = 0; ir < mc; ir += SMR) {
+              const int mr = (mc - ir) < SMR ? (int)(mc - ir) : SMR;
+              float* cp = c + (ic + ir) * n + jc + jr;
+              int32_t* ip = argmax + (ic + ir) * n + jc + jr;
+              const float* ap = pa + ir * kc;
+              const float* bp = pb + jr * kc;
+              __m256 acc[SMR];
+              __m256i idx[SMR];
+              for (int i = 0; i < SMR; ++i) {
+                float row[SNR];
+                int32_t irow[SNR];
+                for (int j = 0; j < SNR; ++j) {
+                  const int in = i < mr && j < nr;
+                  row[j] = in ? cp[i * n + j] : z;
+                  irow[j] = in ? ip[i * n + j] : 0;
+                }
+                acc[i] = _mm256_loadu_ps(row);
+                idx[i] = _mm256_loadu_si256((const __m256i*)irow);
+              }
+              for (int64_t p = 0; p < kc; ++p) {
+                const __m256 bv = _mm256_loadu_ps(bp + p * SNR);
+                const __m256i kv = _mm256_set1_epi32((int32_t)(pc + p));
+                for (int i = 0; i < SMR; ++i) {
+                  const __m256 av = _mm256_set1_ps(ap[p * SMR + i]);
+                  const __m256 prod = maxmul ? _mm256_mul_ps(av, bv) : _mm256_add_ps(av, bv);
+                  const __m256 win = minplus ? _mm256_cmp_ps(prod, acc[i], _CMP_LT_OQ)
+                                             : _mm256_cmp_ps(prod, acc[i], _CMP_GT_OQ);
+                  acc[i] = _mm256_blendv_ps(acc[i], prod, win);
+                  idx[i] = _mm256_castps_si256(
+                      _mm256_blendv_ps(_mm256_castsi256_ps(idx[i]), _mm256_castsi256_ps(kv), win));
+                }
+              }
+              for (int i = 0; i < mr; ++i) {
+                float row[SNR];
+                int32_t irow[SNR];
+                _mm256_storeu_ps(row, acc[i]);
+                _mm256_storeu_si256((__m256i*)irow, idx[i]);
+                for (int j = 0; j < nr; ++j) { cp[i * n + j] = row[j]; ip[i * n + j] = irow[j]; }
+              }
+            }
+          }
+        }
+      }
+    }
+    free(pa);
+    free(pb);
+  }
+  return 0;
+#else
+  (void)semiring; (void)m; (void)n; (void)k; (void)a; (void)b; (void)c; (void)argmax; (void)nthreads;
+  return 1;
+#endif
+}
+
+/*
  * Backward reference: ordered sums (row-major, contiguous).
  * want_a: grad_a[i, am[i,j]] += g[i,j] * (maxmul ? b[am, j] : 1)
  * else:   grad_b[am[i,j], j] += g[i,j] * (maxmul ? a[i, am] : 1)

@@ -33,6 +33,7 @@ def lib():
         i64, vp, i32p = ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p
         L.tg_oracle_gemm.argtypes = [ctypes.c_int, ctypes.c_int, i64, i64, i64, vp, vp, vp, i32p, ctypes.c_int]
         L.tg_oracle_blis_argmax_f32.argtypes = [ctypes.c_int, i64, i64, i64, vp, vp, vp, i32p, ctypes.c_int]
+        L.tg_oracle_simd_argmax_f32.argtypes = [ctypes.c_int, i64, i64, i64, vp, vp, vp, i32p, ctypes.c_int]
         L.tg_oracle_simd_maxplus_f32.argtypes = [i64, i64, i64, vp, vp, vp, ctypes.c_int]
         L.tg_oracle_backward.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, i64, i64, i64, vp, i32p, vp, vp]
         _lib = L
@@ -91,6 +92,20 @@ def simd_maxplus_f32(a: np.ndarray, b: np.ndarray, nthreads: int = 1):
     if rc != 0:
         raise RuntimeError("oracle built without AVX2")
     return c
+
+
+def simd_argmax_f32(semiring: str, a: np.ndarray, b: np.ndarray, nthreads: int = 1):
+    """AVX2 argmax path (8x8 vector tiles, strict masked blend); equals blis_argmax_f32 bit for bit."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), dtype=np.float32)
+    am = np.empty((m, n), dtype=np.int32)
+    rc = lib().tg_oracle_simd_argmax_f32(SEMIRINGS[semiring], m, n, k, _ptr(a), _ptr(b), _ptr(c), _ptr(am), nthreads)
+    if rc != 0:
+        raise RuntimeError("oracle built without AVX2")
+    return c, am
 
 
 def backward(semiring: str, want_a: bool, grad_c: np.ndarray, argmax: np.ndarray, k: int, partner=None):

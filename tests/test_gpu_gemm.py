@@ -230,6 +230,24 @@ def test_argmax_improvement_patterns(semi, pattern, k):
 
 
 @pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("dtype,lim", [(np.int64, 1000), (np.int64, 2**62), (np.int32, 2**30)])
+def test_batched_integers_in_and_out_of_range(semi, dtype, lim):
+    """Batched i64 (through the f64 kernel when exact, else the integer kernel)
+    and batched i32 beyond the exact-in-f32 range (exact integer kernel, with
+    wrap-around), values and argmax, with and without argmax."""
+    rng = np.random.default_rng(21)
+    for (bs, m, k, n) in [(3, 40, 70, 33), (2, 129, 260, 131)]:
+        a = rng.integers(-lim, lim, (bs, m, k)).astype(dtype)
+        b = rng.integers(-lim, lim, (bs, k, n)).astype(dtype)
+        for wa in (True, False):
+            c, am = engine(semi, a, b, wa)
+            c0, am0 = oracle(semi, a, b, wa)
+            assert same_bits(c, c0)
+            if wa:
+                assert np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
 def test_i32_out_of_range_falls_back_exactly(semi):
     """Operands beyond the exact-in-f32 range (|x| > 2^23; MaxMul |x| > 4096)
     take the exact integer kernel, including wrap-around on overflow."""

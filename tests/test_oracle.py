@@ -56,6 +56,33 @@ def test_simd_value_path_matches_argmax_path_across_blocks():
     assert np.array_equal(c_simd, c_ref)
 
 
+@pytest.mark.parametrize("name", [n for n in NAMES if "f32" in n and "batched" not in n])
+def test_simd_argmax_path_matches_fixtures(name):
+    """The AVX2 argmax path (8x8 vector tiles, strict masked blend)."""
+    a, b = FIX[name + "__a"], FIX[name + "__b"]
+    c, am = O.simd_argmax_f32(name.split("_")[0], a, b, nthreads=2)
+    assert np.array_equal(c.view(np.uint32), FIX[name + "__c"].view(np.uint32))
+    assert np.array_equal(am, FIX[name + "__argmax"])
+
+
+@pytest.mark.parametrize("semi", ["maxplus", "minplus", "maxmul"])
+def test_simd_argmax_equals_scalar_path(semi):
+    """Past every block size, ragged edges, ties (quantised values), +-inf and
+    NaN entries: values and indices equal the scalar BLIS argmax path."""
+    rng = np.random.default_rng(11)
+    a = np.round(rng.standard_normal((270, 1100)) * 4).astype(np.float32) / 4
+    b = np.round(rng.standard_normal((1100, 263)) * 4).astype(np.float32) / 4
+    a[rng.random(a.shape) < 0.01] = np.inf
+    b[rng.random(b.shape) < 0.01] = -np.inf
+    a[rng.random(a.shape) < 0.005] = np.nan
+    if semi == "maxmul":
+        a, b = np.abs(a), np.abs(b)
+    c_s, am_s = O.simd_argmax_f32(semi, a, b, nthreads=3)
+    c_r, am_r = O.blis_argmax_f32(semi, a, b, nthreads=3)
+    assert np.array_equal(c_s.view(np.uint32), c_r.view(np.uint32))
+    assert np.array_equal(am_s, am_r)
+
+
 def test_known_answer_2x3_3x2():
     """crates/tropical-gemm-cuda/src/lib.rs:1091-1191 (column-major data there, row-major here)."""
     a = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
