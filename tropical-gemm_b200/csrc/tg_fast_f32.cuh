@@ -593,13 +593,23 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
 #pragma unroll
             for (int i = 0; i < 4; ++i) bv[i] = kg + i < p.k ? B[int64_t(kg + i) * p.ldb + gc] : 0.f;
           }
+          // A's four values: one 16-byte load (kg is a multiple of 4 and
+          // AVEC rows are 16-byte aligned) unless the group is K's tail
           const float* ar = A + gr * p.lda + kg;
+          float av4[4];
+          if (AVEC && kg + 4 <= p.k) {
+            const float4 a4 = *reinterpret_cast<const float4*>(ar);
+            av4[0] = a4.x; av4[1] = a4.y; av4[2] = a4.z; av4[3] = a4.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) av4[i] = kg + i < p.k ? ar[i] : 0.f;
+          }
           v = acc[r][c];
           kw = kg;
 #pragma unroll
           for (int i = 3; i >= 0; --i) {
             if (kg + i < p.k) {
-              const float pr = Op::mul(ar[i], bv[i]);
+              const float pr = Op::mul(av4[i], bv[i]);
               if (pr == acc[r][c]) {
                 v = pr;
                 kw = kg + i;
