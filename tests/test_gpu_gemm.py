@@ -414,3 +414,53 @@ def test_short_k_group_tracking_ties(semi, k):
     c0, am0 = oracle(semi, a, b)
     assert same_bits(c, c0)
     assert np.array_equal(am, am0)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+@pytest.mark.parametrize("dtype", [np.float64, np.int64])
+@pytest.mark.parametrize("kind", ["normal", "ties", "increasing", "decreasing", "plateau", "special"])
+def test_wide_argmax_long_k_patterns(semi, dtype, kind):
+    """f64 / i64 argmax at K around multiples of 64 and up to 4100: ties,
+    improvements at every k or only the first, a long plateau, and (f64)
+    +-inf, NaN and signed zeros."""
+    rng = np.random.default_rng(hash((semi, str(dtype), kind)) % 2**32)
+    for (m, k, n) in [(130, 65, 70), (64, 128, 64), (129, 129, 65), (70, 200, 131), (33, 1000, 40), (17, 4100, 9)]:
+        if kind in ("normal", "ties"):
+            a = _data(rng, dtype, (m, k), kind)
+            b = _data(rng, dtype, (k, n), kind)
+        elif kind == "special":
+            if dtype != np.float64:
+                pytest.skip("special values are float")
+            vals = np.array([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, np.nan, 2.0], np.float64)
+            a = rng.choice(vals, (m, k))
+            b = rng.choice(vals, (k, n))
+        else:
+            ramp = np.arange(k)
+            if kind == "decreasing":
+                ramp = -ramp
+            if semi == "minplus":
+                ramp = -ramp
+            if kind == "plateau":
+                ramp = np.zeros(k, np.int64)
+                ramp[k // 3: 2 * k // 3] = 1 if semi != "minplus" else -1
+            base = 3 if semi == "maxmul" else 0   # MaxMul: keep products positive and ordered
+            a = np.tile(ramp - ramp.min() + base + 1 if semi == "maxmul" else ramp, (m, 1)).astype(dtype)
+            b = np.ones((k, n), dtype) * (1 if semi == "maxmul" else 0)
+            b = b.astype(dtype)
+        if semi == "maxmul" and dtype == np.int64 and kind in ("normal",):
+            a, b = a // 10, b // 10   # keep i64 products inside the exact-in-f64 range
+        c, am = engine(semi, a, b)
+        c0, am0 = oracle(semi, a, b)
+        assert same_bits(c, c0), (m, k, n)
+        assert np.array_equal(am, am0), (m, k, n)
+
+
+@pytest.mark.parametrize("semi", SEMIS)
+def test_wide_argmax_batched(semi):
+    """f64 argmax with batches on grid.z and frequent ties."""
+    rng = np.random.default_rng(31)
+    a = rng.integers(-3, 4, (3, 150, 300)).astype(np.float64)
+    b = rng.integers(-3, 4, (3, 300, 90)).astype(np.float64)
+    c, am = engine(semi, a, b)
+    c0, am0 = oracle(semi, a, b)
+    assert same_bits(c, c0) and np.array_equal(am, am0)
