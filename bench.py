@@ -544,7 +544,7 @@ def run_engine(args):
     if not args.no_e2e:
         # e2e through the public API with host buffers (pinned), rank-local
         a_h = torch.from_numpy(a_np).pin_memory()
-        b_h = torch.from_numpy(b_np).pin_memory()
+        b_h = torch.from_numpy(b_np).pin_memory() if rank == 0 else None
         c_h = torch.empty((M * N_,), dtype=torch.float32).pin_memory()
         am_h = torch.empty((M * N_,), dtype=torch.int32).pin_memory()
         e2e_steps = max(3, args.steps)
@@ -565,7 +565,8 @@ def run_engine(args):
             with torch.cuda.stream(s_in):
                 s_in.wait_event(sl["ev_comp"])            # compute of step i-2 is done with these buffers
                 sl["da"].copy_(a_h.view(M, K), non_blocking=True)
-                sl["db"].copy_(b_h.view(K, N_), non_blocking=True)
+                if rank == 0:   # other ranks receive B over NVLink (the broadcast below)
+                    sl["db"].copy_(b_h.view(K, N_), non_blocking=True)
                 sl["ev_in"].record(s_in)
             stream.wait_event(sl["ev_in"])
             if dist is not None:
@@ -651,8 +652,10 @@ def run_engine(args):
                          if mix_smem else None,
                          "smem_fed_basis": (f"the same pair with its B operands reloaded from shared memory every "
                                             f"iteration: {mix_smem:.1f} products/clk/SM") if mix_smem else None},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * (M * K + K * N_),
-                    "d2h_bytes_per_step": 8 * M * N_, "api": "tropical_gemm.maxplus_matmul_dlpack"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    # whole job: every rank's A shard and rank 0's B in, every rank's C + argmax out
+                    "h2d_bytes_per_step": 4 * (M * K * world + K * N_),
+                    "d2h_bytes_per_step": 8 * M * N_ * world, "api": "tropical_gemm.maxplus_matmul_dlpack"},
             "gpu_launches": args.steps * launches_per_call(M, N_, K, props.multi_processor_count),
             "clocks": clocks,
             "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
