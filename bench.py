@@ -284,7 +284,7 @@ def extras(dev):
     return res
 
 
-CASES = ("backward", "f64", "f64_values", "apsp_step", "minplus_inf", "pipe_rates")
+CASES = ("backward", "batched_fwd", "f64", "f64_values", "apsp_step", "minplus_inf", "pipe_rates")
 
 PIPE_VARIANTS = ("pair_fadd2_fmnmx3", "fadd2_alone", "fmnmx3_alone", "fadd_alone", "fmnmx_alone",
                  "fadd_x2_fmnmx3", "fadd2_fmnmx_x2", "fadd_fmnmx", "engine_ktile_body",
@@ -346,6 +346,14 @@ def run_case(args):
         alg = 2 * bs * m * n * 8 + bs * (m * k + k * n) * 4
         out.update({"ms": ms, "algorithmic_bytes": alg, "gbs": alg / (ms * 1e-3) / 1e9,
                     "config": {"batch": bs, "m": m, "k": k, "n": n, "dtype": "f32"}})
+    elif args.case == "batched_fwd":
+        # BASELINE config 3 forward: MaxPlus f32 + argmax, batch 64 of [512x256].[256x512]
+        bs, m, k, n = 64, 512, 256, 512
+        a = torch.from_numpy(rng.standard_normal((bs, m, k), dtype=np.float32)).to(dev)
+        b = torch.from_numpy(rng.standard_normal((bs, k, n), dtype=np.float32)).to(dev)
+        ms = _time_ms(lambda: Nat.gemm_batched("maxplus", a, b, True), reps=args.steps, warm=args.warmup)
+        out.update({"ms": ms, "ops_per_s": float(bs) * m * n * k / (ms * 1e-3),
+                    "config": {"batch": bs, "m": m, "k": k, "n": n, "dtype": "f32", "argmax": True}})
     elif args.case in ("f64", "f64_values"):
         sz = args.size if args.size != 8192 else 4096
         a = torch.rand((sz, sz), dtype=torch.float64, device=dev)
@@ -665,7 +673,7 @@ def run_engine(args):
         if config5 is not None:
             out["config5_sharded_32768x32768x8192"] = config5
         if world == 1 and not args.no_cpu:
-            rows = args.cpu_rows
+            rows = args.cpu_baseline_rows
             threads = os.cpu_count() or 1
             v, dt = cpu_baseline(rows, threads)
             out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
@@ -837,7 +845,9 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    p.add_argument("--cpu-rows", type=int, default=1024)
+    p.add_argument("--cpu-rows", type=int, default=1024, help="rows of A per step of the reference arm")
+    p.add_argument("--cpu-baseline-rows", type=int, default=8192,
+                   help="rows of A timed in the engine line's cpu_baseline (8192 = the whole workload)")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-extras", action="store_true", help="skip the other BASELINE configs (extra keys)")
