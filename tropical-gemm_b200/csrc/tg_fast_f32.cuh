@@ -414,13 +414,17 @@ __device__ __forceinline__ void tile_math(const float* a_stage, const float* b_s
 // records the group of the last strict improvement -- 6 instructions per 4
 // products (values only: 4).  The epilogue resolves the winning k inside
 // that group from A (global) and B (the resident panel, or global).
-template <int S>
+// UNROLL: 4-k groups per unrolled body.  The whole k-tile (8) for K > 256;
+// 2 for the resident-panel kernel (K <= 256), whose epilogue and k loop do
+// not fit the instruction cache together (no-instruction stalls 0.65 per
+// issue fully unrolled; config 3 forward 0.540 -> 0.526 ms).
+template <int S, int UNROLL = 8>
 __device__ __forceinline__ void tile_math_g4(const float* a_stage, const float* b_stage, int wm, int wn, int lm,
                                              int ln, float (&acc)[8][8], int32_t (&pidx)[8][8], int64_t kbase) {
   using Op = FastOps<S>;
   const float* Ap = a_stage + (wm * 32 + lm) * kFApitch;
   const float* Bp = b_stage + (wn * 64 + 2 * ln) * 2;
-#pragma unroll
+#pragma unroll UNROLL
   for (int k4 = 0; k4 < kFBK; k4 += 4) {
     float4 a[8];
 #pragma unroll
@@ -541,7 +545,7 @@ fast_f32_kernel(GemmArgs p, int tiles_per_chunk, int b_vec, float acc_init, cons
       if (nt < ktiles) load_tile(int(nt % kFStages), nt);
       cp_async_commit();
     }
-    if constexpr (PAIR) tile_math_g4<S>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
+    if constexpr (PAIR) tile_math_g4<S, BPANEL ? 2 : 8>(stage, bstage, wm, wn, lm, ln, acc, pidx, t * kFBK);
     else tile_math<S>(stage, bstage, wm, wn, lm, ln, acc);
     if (ARGMAX && !PAIR && ((t + 1) % tiles_per_chunk == 0 || t == ktiles - 1)) {
       // chunk boundary: remember the chunk of each output's latest strict improvement
