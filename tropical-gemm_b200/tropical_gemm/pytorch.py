@@ -71,7 +71,9 @@ class _TropicalMatmulBase(torch.autograd.Function):
     def backward(cls, ctx, grad_c: torch.Tensor):
         saved = ctx.saved_tensors
         am = saved[0]
+        # contiguous once for both gradients (sum().backward() hands in a stride-0 expansion)
         g = grad_c.to(device=am.device, dtype=saved[1].dtype if len(saved) > 1 else _compute_dtype(grad_c))
+        g = g.contiguous()
         if cls.SEMIRING == "maxmul":
             _, ad, bd = saved
             ga = N.backward("maxmul", True, g, am, ctx.k, bd) if ctx.needs_input_grad[0] else None
