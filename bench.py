@@ -142,13 +142,13 @@ def profile_traffic():
 def launches_per_call(m: int, n: int, k: int, sms: int) -> int:
     """Kernels one f32 argmax tg_gemm call enqueues: the persistent fused
     kernel (taken for K >= 8192 with at least 16 128x128 tiles per SM, K <=
-    65536, aligned rows) runs after two copies of B are made (3 launches);
+    65536, aligned rows) runs after one kernel writes both copies of B it reads (2 launches);
     the chunk kernel alone is 1."""
     env = os.environ.get("TROPICAL_GEMM_ARGMAX_FUSED", "")
     tiles = ((m + 127) // 128) * ((n + 127) // 128)
     auto = 8192 <= k and tiles >= 16 * sms
     fused = k <= 65536 and k > 1024 and n % 4 == 0 and k % 4 == 0 and (env == "1" or (env != "0" and auto))
-    return 3 if fused else 1
+    return 2 if fused else 1
 
 
 def cpu_baseline(rows: int, threads: int):

@@ -14,8 +14,8 @@
 //  * each pipeline stage holds A's k-tile (16-byte cp.async by every
 //    thread), B's k-tile (one TMA box of a k-pair-interleaved copy of B) and
 //    the previous tile's columns of B for the same k (one TMA box of a
-//    transposed copy of B, 128-byte swizzled); both copies are made before
-//    the launch;
+//    transposed copy of B, 128-byte swizzled); both copies are made by one
+//    pass over B (copy_b_kernel) before the launch;
 //  * while k-tile t of tile i is folded, the outputs of tile i-1 whose
 //    chunk is t's are scanned from the same stage -- A is shared because
 //    both tiles lie in one row panel -- so the chunk kernel's post-loop
@@ -44,43 +44,34 @@ static_assert(kXOffBar % 8 == 0 && kXOffCnt % 4 == 0, "barrier / counter alignme
 static_assert((kXStageFloats * 4) % 1024 == 0 && (kFAStage * 4) % 128 == 0 && (kXBprev * 4) % 1024 == 0,
               "TMA destinations");
 
-// B (K x N, ldb, batch stride sb) -> k-pair-interleaved copy [K2][np][2]
-// (K2 = ceil(K/2), np >= N a multiple of 4; zeros outside B).
-static __global__ void interleave_b_kernel(const float* __restrict__ b, int64_t k, int64_t n, int64_t ldb, int64_t sb,
-                                           float* __restrict__ out, int64_t np) {
-  const int64_t k2n = (k + 1) / 2;
-  const float* bb = b + int64_t(blockIdx.y) * sb;
-  float2* o = reinterpret_cast<float2*>(out + int64_t(blockIdx.y) * k2n * np * 2);
-  const int64_t total = k2n * np;
-  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t k2 = e / np, c = e - k2 * np;
-    float2 v = make_float2(0.f, 0.f);
-    if (c < n) {
-      v.x = bb[(2 * k2) * ldb + c];
-      if (2 * k2 + 1 < k) v.y = bb[(2 * k2 + 1) * ldb + c];
-    }
-    o[e] = v;
-  }
-}
-
-// B (K x N) -> transposed copy [N][kp] (kp >= K a multiple of 4), one
-// 32 x 32 block per CTA through shared memory; columns k >= K are zero.
-static __global__ void transpose_b_kernel(const float* __restrict__ b, int64_t k, int64_t n, int64_t ldb, int64_t sb,
-                                          float* __restrict__ out, int64_t kp) {
+// Both copies of B the kernel reads, from one pass over B (K x N, ldb, batch
+// stride sb) in 32 x 32 blocks staged through shared memory:
+//  * il: k-pair-interleaved [K2][np][2] (K2 = ceil(K/2), np >= N a multiple
+//    of 4), coalesced float2 stores along n;
+//  * bt: transposed [N][kp] (kp >= K a multiple of 4), coalesced along k.
+// Everything outside B is zero.  Grid: (ceil(np/32), k blocks, batch).
+static __global__ void copy_b_kernel(const float* __restrict__ b, int64_t k, int64_t n, int64_t ldb, int64_t sb,
+                                     float* __restrict__ il, int64_t np, float* __restrict__ bt, int64_t kp) {
   __shared__ float blk[32][33];
+  const int64_t k2n = (k + 1) / 2;
   const float* bb = b + int64_t(blockIdx.z) * sb;
-  float* ob = out + int64_t(blockIdx.z) * n * kp;
+  float2* ilb = reinterpret_cast<float2*>(il + int64_t(blockIdx.z) * k2n * np * 2);
+  float* btb = bt + int64_t(blockIdx.z) * n * kp;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 256 threads: 8 rows per pass
+  const int64_t n0 = int64_t(blockIdx.x) * 32;
   for (int64_t k0 = int64_t(blockIdx.y) * 32; k0 < kp; k0 += int64_t(gridDim.y) * 32) {
-    const int64_t n0 = int64_t(blockIdx.x) * 32;
     for (int r = ty; r < 32; r += 8) {
       const int64_t kk = k0 + r, nn = n0 + tx;
       blk[r][tx] = (kk < k && nn < n) ? bb[kk * ldb + nn] : 0.f;
     }
     __syncthreads();
-    for (int r = ty; r < 32; r += 8) {
+    for (int r = ty; r < 32; r += 8) {   // transposed: row n0 + r, k = k0 + tx
       const int64_t nn = n0 + r, kk = k0 + tx;
-      if (nn < n && kk < kp) ob[nn * kp + kk] = blk[tx][r];
+      if (nn < n && kk < kp) btb[nn * kp + kk] = blk[tx][r];
+    }
+    for (int r = ty; r < 16; r += 8) {   // interleaved: k-pair row k0/2 + r, column n0 + tx
+      const int64_t k2 = k0 / 2 + r, c = n0 + tx;
+      if (k2 < k2n && c < np) ilb[k2 * np + c] = make_float2(blk[2 * r][tx], blk[2 * r + 1][tx]);
     }
     __syncthreads();
   }

@@ -85,19 +85,14 @@ tg_status launch_argmax_fused(const Problem& P, cudaStream_t st, float acc_init)
     return TG_ERR_UNSUPPORTED;
   }
   {
-    const int64_t total = k2 * np;
-    const unsigned gx = unsigned(std::min<int64_t>((total + 255) / 256, 4 * int64_t(sm_count())));
-    tg::interleave_b_kernel<<<dim3(gx, unsigned(P.batch)), 256, 0, st>>>(static_cast<const float*>(g.b), g.k, g.n,
-                                                                         g.ldb, g.sb, bil, np);
-    tg_status s = check_launch("interleave_b_kernel launch");
-    if (s == TG_OK) {
-      const int64_t bx = (g.n + 31) / 32, by = std::min<int64_t>((kp + 31) / 32, 65535);
-      if (bx > 0x7fffffff) s = fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
-      else {
-        tg::transpose_b_kernel<<<dim3(unsigned(bx), unsigned(by), unsigned(P.batch)), 256, 0, st>>>(
-            static_cast<const float*>(g.b), g.k, g.n, g.ldb, g.sb, bt, kp);
-        s = check_launch("transpose_b_kernel launch");
-      }
+    // one pass over B writes both copies (32 x 32 blocks over n < np, k < kp)
+    const int64_t bx = (np + 31) / 32, by = std::min<int64_t>((kp + 31) / 32, 65535);
+    tg_status s = TG_OK;
+    if (bx > 0x7fffffff) s = fail(TG_ERR_UNSUPPORTED, "problem too large for one launch");
+    else {
+      tg::copy_b_kernel<<<dim3(unsigned(bx), unsigned(by), unsigned(P.batch)), 256, 0, st>>>(
+          static_cast<const float*>(g.b), g.k, g.n, g.ldb, g.sb, bil, np, bt, kp);
+      s = check_launch("copy_b_kernel launch");
     }
     if (s != TG_OK) {
       scratch_free(ws, st);
